@@ -1,0 +1,530 @@
+"""Benchmark of the hyper-connections hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}]
+
+Headline workload (one "step" = one forward + one backward of the fused
+hyper-connection step over one batch): x [16,1024,4,768] bf16 streams, f
+[16,1024,768] bf16 layer output, per-token H [.,4,4] = expm(skew), alpha/beta
+= softmax, all float32, upstream gradients ~ N(0,1); seeded synthetic data
+(the reference publishes no dataset for this path).
+
+Metric: algorithmic HBM bytes of the fused forward + backward per second,
+where every tensor is counted once:
+  fwd  T*((2nD + 2D)*2 + (n^2 + 2n)*4)  bytes  (read x, f, H, alpha, beta; write u, x_out)
+  bwd  T*((3nD + 3D)*2 + 2(n^2 + 2n)*4) bytes  (read g_u, g_x, x, f, H, alpha, beta;
+                                                write grad_x, grad_f, grad_H, grad_alpha, grad_beta)
+The batched matrix exponential (65,536 skew 4x4, forward + Frechet backward)
+is reported alongside in matrices/s.
+
+Timing: CUDA events on the launching stream around each kernel, L2 flushed
+(a 256 MiB write) between steps outside the events, barrier + synchronize
+around the K timed steps, max over ranks. Under torchrun every rank runs the
+full workload on its own GPU with no collective on the data path (weak
+scaling); value = N * bytes / max-rank time.
+
+``--impl reference`` times the reference's own CPU path for the same work
+(read einsum -> write einsum -> eager stream mix under bf16 autocast, with
+autograd backward; hyperconnections/cghc.py:410, :417, :365-392) on a bounded
+sample of tokens with every host thread, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import threading
+import time
+
+import numpy as np
+import torch
+
+METRIC = "stream-mix fwd+bwd HBM GB/s (% of 8 TB/s); batched expm matrices/sec"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+# ---------------------------------------------------------------- workloads
+BATCH, SEQ, N_STREAMS, BLOCK = 16, 1024, 4, 768
+TOKENS = BATCH * SEQ
+EXPM_BATCH, EXPM_N = 65536, 4
+REF_TOKENS = 1024  # tokens per step of the reference arm's bounded CPU sample
+
+
+def fused_bytes(T: int, n: int, D: int, esize: int = 2) -> tuple[int, int]:
+    """Algorithmic bytes (each tensor touched once) of the fused fwd and bwd."""
+    small = (n * n + 2 * n) * 4
+    fwd = T * ((2 * n * D + 2 * D) * esize + small)
+    bwd = T * ((3 * n * D + 3 * D) * esize + 2 * small)
+    return fwd, bwd
+
+
+def fused_workload(T: int, n: int, D: int, dtype=torch.bfloat16, seed: int = 0):
+    """x, f, H, alpha, beta, g_u, g_x drawn in this order from one CPU generator:
+    x, f ~ N(0,1); H = expm(S - S^T), S = strict upper triangle of 0.5*N(0,1)
+    (a skew-symmetric generator whose off-diagonal entries are N(0, 0.5^2));
+    alpha, beta = softmax of N(0,1) logits; g_u, g_x ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, n, D, generator=g).to(dtype)
+    f = torch.randn(T, D, generator=g).to(dtype)
+    S = torch.triu(0.5 * torch.randn(T, n, n, generator=g), 1)
+    H = torch.linalg.matrix_exp(S - S.mT).contiguous()
+    alpha = torch.softmax(torch.randn(T, n, generator=g), -1)
+    beta = torch.softmax(torch.randn(T, n, generator=g), -1)
+    g_u = torch.randn(T, D, generator=g).to(dtype)
+    g_x = torch.randn(T, n, D, generator=g).to(dtype)
+    return x, f, H, alpha, beta, g_u, g_x
+
+
+def expm_workload(B: int, n: int, seed: int = 0):
+    """A = 0.5 (G - G^T) / 2 with G ~ N(0,1), then an upstream gradient ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    M = torch.randn(B, n, n, generator=g)
+    A = (0.5 * (M - M.mT) / 2).contiguous()
+    G = torch.randn(B, n, n, generator=g)
+    return A, G
+
+
+# ---------------------------------------------------------------- clocks
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read-only) in a
+    background thread; ``window(t0, t1)`` summarises the samples taken while
+    the timed region ran."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[float, int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(visible.split(",")[device_index]) if visible else device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML missing: report no clocks rather than guess
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def window(self, t0: float, t1: float) -> dict:
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside:  # very short windows: take the nearest samples
+            inside = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mask = 0
+        for s in inside:
+            mask |= s[2]
+        reasons = [name for bit, name in _REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {
+            "sm_mhz": float(np.median([s[1] for s in inside])),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": reasons,
+            "samples": len(inside),
+        }
+
+
+# ---------------------------------------------------------------- helpers
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh).get(kernel)
+    except Exception:
+        return None
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+# ---------------------------------------------------------------- B200 arm
+class FusedRunner:
+    """Direct C-ABI launches of the fused forward and backward on resident
+    device buffers (the kernels timed for ``value``)."""
+
+    def __init__(self, device, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0):
+        from hyperconnections_b200 import _lib
+
+        self.lib = _lib.lib()
+        self.T, self.n, self.D = T, n, D
+        host = fused_workload(T, n, D, seed=seed)
+        self.x, self.f, self.H, self.alpha, self.beta, self.g_u, self.g_x = [t.to(device) for t in host]
+        dt = self.x.dtype
+        self.u = torch.empty(T, D, dtype=dt, device=device)
+        self.x_out = torch.empty_like(self.x)
+        self.grad_x = torch.empty_like(self.x)
+        self.grad_f = torch.empty(T, D, dtype=dt, device=device)
+        self.grad_H = torch.empty(T, n, n, device=device)
+        self.grad_a = torch.empty(T, n, device=device)
+        self.grad_b = torch.empty(T, n, device=device)
+        self.code = _lib.dtype_code(dt)
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        self._check = _lib.check
+
+    def fwd(self):
+        rc = self.lib.hc_fused_fwd(
+            self.x.data_ptr(), self.f.data_ptr(), self.H.data_ptr(), self.alpha.data_ptr(),
+            self.beta.data_ptr(), self.u.data_ptr(), self.x_out.data_ptr(), self.T, self.n, self.D,
+            self.code, self.stream)
+        self._check(rc, "hc_fused_fwd")
+
+    def bwd(self):
+        rc = self.lib.hc_fused_bwd(
+            self.g_u.data_ptr(), self.g_x.data_ptr(), self.x.data_ptr(), self.f.data_ptr(),
+            self.H.data_ptr(), self.alpha.data_ptr(), self.beta.data_ptr(), self.grad_x.data_ptr(),
+            self.grad_f.data_ptr(), self.grad_H.data_ptr(), self.grad_a.data_ptr(), self.grad_b.data_ptr(),
+            self.T, self.n, self.D, self.code, self.stream)
+        self._check(rc, "hc_fused_bwd")
+
+
+def time_fused(device, steps, warmup, world):
+    runner = FusedRunner(device)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for _ in range(warmup):
+        flush.fill_(1.0)
+        runner.fwd()
+        runner.bwd()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        flush.fill_(float(i))  # evict L2 between steps, outside the events
+        e = evs[i]
+        e[0].record()
+        runner.fwd()
+        e[1].record()
+        runner.bwd()
+        e[2].record()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    t1 = time.perf_counter()
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    del flush
+    return {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t1), "launches": 2 * steps}
+
+
+def time_expm(device, steps, warmup):
+    from hyperconnections_b200.ops import expm_t18
+
+    A, G = (t.to(device) for t in expm_workload(EXPM_BATCH, EXPM_N))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step():
+        a = A.detach().requires_grad_(True)
+        E = expm_t18(a)
+        E.backward(G)
+        return a.grad
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    ms = []
+    for i in range(steps):
+        flush.fill_(float(i))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms.append(e0.elapsed_time(e1))
+    del flush
+    return ms
+
+
+def time_e2e(device, steps, warmup):
+    """The same fused step through the public API (autograd) with inputs in
+    pinned host memory: every step copies its inputs host->device and reads
+    every output back device->host."""
+    from hyperconnections_b200.ops import stream_mix_fused
+
+    host = [t.pin_memory() for t in fused_workload(TOKENS, N_STREAMS, BLOCK, seed=1)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    outs_host = None
+
+    def step():
+        nonlocal outs_host
+        x, f, H, a, b, g_u, g_x = (t.to(device, non_blocking=True) for t in host)
+        leaves = [t.requires_grad_(True) for t in (x, f, H, a, b)]
+        u, x_out = stream_mix_fused(*leaves)
+        torch.autograd.backward([u, x_out], [g_u, g_x])
+        outs = [u, x_out] + [t.grad for t in leaves]
+        if outs_host is None:
+            outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+        for dst, src in zip(outs_host, outs):
+            dst.copy_(src.detach(), non_blocking=True)
+        return sum(o.numel() * o.element_size() for o in outs)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    d2h = 0
+    for _ in range(steps):
+        d2h = step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1) / steps, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_fused_sample(tokens: int, budget_s: float, min_reps: int = 3):
+    """The reference's CPU path (oracle.torch_ref) on `tokens` tokens of the
+    workload; returns (median seconds per rep, reps, threads)."""
+    from oracle.torch_ref import fused_step_cpu
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, f, H, a, b, g_u, g_x = fused_workload(tokens, N_STREAMS, BLOCK, seed=2)
+    fused_step_cpu(x, f, H, a, b, g_u, g_x)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_reps or (time.perf_counter() - t_start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        fused_step_cpu(x, f, H, a, b, g_u, g_x)
+        times.append(time.perf_counter() - t0)
+    return float(np.median(times)), len(times), torch.get_num_threads()
+
+
+def cpu_expm_sample(batch: int, budget_s: float, min_reps: int = 3):
+    from oracle.torch_ref import expm_t18_cpu
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    A, G = expm_workload(batch, EXPM_N, seed=3)
+    expm_t18_cpu(A, G)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_reps or (time.perf_counter() - t_start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        expm_t18_cpu(A, G)
+        times.append(time.perf_counter() - t0)
+    return float(np.median(times)), len(times), torch.get_num_threads()
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+CONFIG = {
+    "workload": "fused hyper-connection step fwd+bwd: x[16,1024,4,768] bf16, f[16,1024,768] bf16, "
+                "H[16,1024,4,4]=expm(skew) fp32, alpha/beta[16,1024,4]=softmax fp32, seed 0",
+    "tokens": TOKENS, "n_streams": N_STREAMS, "block_size": BLOCK,
+    "l2": "flushed between steps (256 MiB write, outside the timed events)",
+}
+
+
+def run_reference(args):
+    """The reference arm: W untimed + K timed steps of the reference's CPU
+    path, each step a bounded sample of the workload (REF_TOKENS tokens)."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle.torch_ref import fused_step_cpu
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = REF_TOKENS
+    x, f, H, a, b, g_u, g_x = fused_workload(tokens, N_STREAMS, BLOCK, seed=2)
+    for _ in range(args.warmup):
+        fused_step_cpu(x, f, H, a, b, g_u, g_x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fused_step_cpu(x, f, H, a, b, g_u, g_x)
+    sec = (time.perf_counter() - t0) / args.steps
+    fb, bb = fused_bytes(tokens, N_STREAMS, BLOCK)
+    gbs = (fb + bb) / sec / 1e9
+    sample = (f"{tokens} of {TOKENS} tokens of the workload per step, {args.steps} steps "
+              f"(reference eager CPU path: einsum read/write + eager mix, bf16 autocast, autograd backward)")
+    line = {
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": dict(CONFIG, sample_tokens=tokens), "impl": "reference",
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    world, rank, local = dist_env()
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    from hyperconnections_b200 import _lib
+
+    _lib.lib()  # fail loudly when the kernels are missing
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    res = time_fused(device, args.steps, args.warmup, world)
+    t0, t1 = res["wall"]
+    clocks = sampler.window(t0, t1)
+
+    fwd_ms = float(np.mean(res["fwd_ms"]))
+    bwd_ms = float(np.mean(res["bwd_ms"]))
+    step_ms = fwd_ms + bwd_ms
+    step_ms_max = max_over_ranks(step_ms, world, device)
+    fb, bb = fused_bytes(TOKENS, N_STREAMS, BLOCK)
+    value = world * (fb + bb) / (step_ms_max * 1e-3) / 1e9
+
+    expm_ms = time_expm(device, max(5, min(args.steps, 50)), max(3, args.warmup))
+    expm_step = float(np.mean(expm_ms))
+    expm_step_max = max_over_ranks(expm_step, world, device)
+    expm_rate = world * EXPM_BATCH / (expm_step_max * 1e-3)
+
+    e2e_ms, h2d, d2h = time_e2e(device, max(3, min(args.steps, 10)), 2)
+    e2e_ms_max = max_over_ranks(e2e_ms, world, device)
+    e2e_value = world * (fb + bb) / (e2e_ms_max * 1e-3) / 1e9
+    sampler.stop()
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        dom_name, dom_ms, dom_bytes = ("hc_fused_bwd", bwd_ms, bb) if bwd_ms >= fwd_ms else ("hc_fused_fwd", fwd_ms, fb)
+        achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms_max,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded)",
+            "config": CONFIG,
+            "pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
+            "pct_of_measured_hbm": 100.0 * value / world / peak,
+            "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms},
+            "roofline": {
+                "bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak,
+                "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": committed_traffic(dom_name), "algorithmic_bytes": dom_bytes,
+            },
+            "expm": {"metric": "batched expm fwd+bwd matrices/s", "value": expm_rate, "unit": "matrices/s",
+                     "ms_per_step": expm_step_max, "batch": EXPM_BATCH, "n": EXPM_N,
+                     "scaling": "global (reference semantics)"},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_ms_max,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "hyperconnections_b200.ops.stream_mix_fused + autograd, pinned host buffers"},
+            "gpu_launches": res["launches"],
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            tokens = 2048
+            sec, reps, threads = cpu_fused_sample(tokens, budget_s=12.0)
+            fb_s, bb_s = fused_bytes(tokens, N_STREAMS, BLOCK)
+            line["cpu_baseline"] = {
+                "value": (fb_s + bb_s) / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{tokens} of {TOKENS} tokens per rep, median of {reps} reps "
+                          "(reference eager CPU path: einsum read/write + eager mix, bf16 autocast, autograd)",
+                "cpu": cpu_model(),
+            }
+            esec, ereps, ethreads = cpu_expm_sample(EXPM_BATCH, budget_s=8.0)
+            line["expm"]["cpu_baseline"] = {
+                "value": EXPM_BATCH / esec, "unit": "matrices/s", "cores": ethreads, "kind": "port",
+                "sample": f"{EXPM_BATCH} matrices per rep, median of {ereps} reps (eager expm_t18 body + autograd)",
+            }
+            line["expm"]["speedup_vs_cpu"] = expm_rate / (EXPM_BATCH / esec)
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,118 @@
+"""ctypes binding of libhcops.so, the C ABI declared in include/hcops.h.
+
+This module is the only place that touches the shared library. It resolves
+every entry point once, fixes its argument types, and turns non-zero status
+codes into RuntimeError. There is deliberately no fallback: when the library
+is missing or a tensor is not on a CUDA device, the callers in
+``hyperconnections_b200.ops`` raise instead of computing anything elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhcops.so")
+
+HC_DTYPE_F32 = 0
+HC_DTYPE_F16 = 1
+HC_DTYPE_BF16 = 2
+
+_DTYPE_CODE = {
+    torch.float32: HC_DTYPE_F32,
+    torch.float16: HC_DTYPE_F16,
+    torch.bfloat16: HC_DTYPE_BF16,
+}
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/hcops.h
+_SIGNATURES = {
+    "hc_error_string": (ctypes.c_char_p, [_c_int]),
+    "hc_abi_version": (_c_int, []),
+    "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
+    "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
+    "hc_expm_t18_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
+    "hc_expm_pade_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp]),
+    "hc_expm_pade_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp]),
+    "hc_stream_mix_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_i64, _c_int, _c_int, _vp]),
+    "hc_stream_mix_bwd": (
+        _c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_i64, _c_int, _c_int, _vp],
+    ),
+    "hc_fused_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_i64, _c_int, _vp]),
+    "hc_fused_bwd": (
+        _c_int,
+        [_vp] * 12 + [_c_i64, _c_int, _c_i64, _c_int, _vp],
+    ),
+}
+
+EXPECTED_ABI_VERSION = 1
+
+_lib: Optional[ctypes.CDLL] = None
+_load_error: Optional[str] = None
+
+
+def _load() -> Optional[ctypes.CDLL]:
+    global _lib, _load_error
+    if _lib is not None or _load_error is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        _load_error = f"{LIB_PATH} is not built (run `make -C hyperconnections_b200/csrc`)"
+        return None
+    try:
+        lib = ctypes.CDLL(LIB_PATH)
+    except OSError as exc:  # pragma: no cover - depends on the environment
+        _load_error = f"cannot load {LIB_PATH}: {exc}"
+        return None
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.hc_abi_version() != EXPECTED_ABI_VERSION:
+        _load_error = "libhcops.so ABI version mismatch; rebuild it"
+        return None
+    _lib = lib
+    return _lib
+
+
+def available() -> bool:
+    """True when libhcops.so is present and loadable."""
+    return _load() is not None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises RuntimeError when it is unavailable."""
+    handle = _load()
+    if handle is None:
+        raise RuntimeError(f"hyperconnections_b200 CUDA kernels unavailable: {_load_error}")
+    return handle
+
+
+def check(rc: int, what: str) -> None:
+    """Raise RuntimeError for a non-zero hcops status code."""
+    if rc != 0:
+        msg = lib().hc_error_string(rc).decode()
+        raise RuntimeError(f"{what} failed: {msg} (hcops status {rc})")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16") from None
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    """Device address of a tensor (None stays None -> NULL)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    """Raw cudaStream_t of torch's current stream on the tensor's device."""
+    return torch.cuda.current_stream(t.device).cuda_stream

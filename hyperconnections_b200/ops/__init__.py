@@ -1,0 +1,11 @@
+"""Hot-path operators with the reference's import path and names
+(hyperconnections/ops/__init__.py:1-4), plus the fused step and the Pade
+matrix exponential."""
+
+from .expm import expm_t18, matrix_exp
+from .fused import stream_mix_fused
+from .stream_mix import HAS_TRITON, stream_mix_add
+
+HAS_KERNELS = HAS_TRITON
+
+__all__ = ["HAS_TRITON", "HAS_KERNELS", "stream_mix_add", "expm_t18", "matrix_exp", "stream_mix_fused"]

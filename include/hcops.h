@@ -1,0 +1,156 @@
+/*
+ * hcops.h — C ABI of libhcops.so, the sm_100a kernels of the hyper-connections
+ * hot path (batched small-matrix exponential and fused stream mixing).
+ *
+ * Every entry point:
+ *   - takes DEVICE pointers, element counts and a cudaStream_t passed as void*
+ *     (NULL = legacy default stream);
+ *   - enqueues its kernels on that stream and returns without synchronising;
+ *   - allocates nothing and keeps no state between calls (scratch memory, where
+ *     a path needs it, is passed in by the caller);
+ *   - returns HC_OK (0) or one of the HC_ERR_* codes below; hc_error_string()
+ *     turns a code into text.
+ *
+ * Layouts are dense row-major with the token (batch) index outermost:
+ *   streams  x, Y, out, grad_out, grad_x   [T, n, D]   stream dtype
+ *   layer output f, read output u           [T, D]      stream dtype
+ *   mixing matrix Phi / H                   [T, n, n]   param dtype
+ *   projection direction v                  [T, n]      param dtype
+ *   read weights alpha, write weights beta  [T, n]      float32
+ *   matrices for expm A, E, G, dA           [batch, n, n] float32
+ * All gradients of per-token parameters are written as float32.
+ *
+ * Citations name the reference interface each entry point replaces
+ * (pjjajal/hyperconnections, paths relative to the project root).
+ */
+#ifndef HCOPS_H
+#define HCOPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define HC_OK                 0
+#define HC_ERR_NULL_POINTER   1  /* a required pointer is NULL                     */
+#define HC_ERR_BAD_SIZE       2  /* negative size, or n / D out of range           */
+#define HC_ERR_UNSUPPORTED_N  3  /* n outside 1..8                                 */
+#define HC_ERR_DTYPE          4  /* unknown dtype code or unsupported combination  */
+#define HC_ERR_ALIGNMENT      5  /* a float32 pointer is not 4-byte aligned        */
+#define HC_ERR_SCRATCH        6  /* scratch buffer missing or too small            */
+#define HC_ERR_LAUNCH         7  /* the CUDA launch itself failed                  */
+
+/* ---- dtype codes ---------------------------------------------------------- */
+#define HC_DTYPE_F32   0
+#define HC_DTYPE_F16   1
+#define HC_DTYPE_BF16  2
+
+/* Text for a status code (static storage). */
+const char* hc_error_string(int code);
+
+/* Library ABI version; bumped whenever a signature below changes. */
+int hc_abi_version(void);
+
+/* ===========================================================================
+ * Batched matrix exponential, n <= 8, float32.
+ * ======================================================================== */
+
+/* Number of float32 words of scratch that hc_expm_t18_fwd / hc_expm_t18_bwd
+ * need in global-scaling mode for a batch of `batch` matrices of order n
+ * (the per-block partial maxima of ||A||_1). Returns 0 in error cases. */
+int64_t hc_expm_t18_scratch_words(int64_t batch, int n);
+
+/* E = exp(A) by the optimised Taylor polynomial of degree 18 (Bader, Blanes
+ * and Casas 2019) with scaling and squaring, theta_18 = 3.01.
+ *   per_matrix == 0: ONE scaling exponent for the whole batch, taken from
+ *     max_b ||A_b||_1, as the reference does; `scratch` must hold
+ *     hc_expm_t18_scratch_words(batch, n) floats.
+ *   per_matrix != 0: each matrix gets its own exponent; scratch may be NULL.
+ * Replaces: hyperconnections/ops/expm.py:69-106 (expm_t18 forward). */
+int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n,
+                    float* scratch, int64_t scratch_words, int per_matrix,
+                    void* stream);
+
+/* dA = L_exp18(A^T, G): the adjoint Frechet derivative of the same T18
+ * approximant (same scaling exponent as the forward), i.e. the gradient of
+ * sum(G * expm_t18(A)) with respect to A.
+ * Replaces: the autograd backward of hyperconnections/ops/expm.py:69-106. */
+int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch,
+                    int n, float* scratch, int64_t scratch_words,
+                    int per_matrix, void* stream);
+
+/* E = exp(A) by diagonal Pade [7/7] with per-matrix scaling and squaring
+ * (Higham 2005, theta_7 = 3.925724783138660 for unit roundoff 2^-24) and an
+ * in-register Gauss-Jordan solve with partial pivoting.
+ * Replaces: torch.linalg.matrix_exp at hyperconnections/cghc.py:321. */
+int hc_expm_pade_fwd(const float* A, float* E, int64_t batch, int n,
+                     void* stream);
+
+/* dA = L_exp(A^T, G) of the Pade approximant (Al-Mohy and Higham 2009).
+ * Replaces: the autograd backward of torch.linalg.matrix_exp at
+ * hyperconnections/cghc.py:321. */
+int hc_expm_pade_bwd(const float* A, const float* G, float* dA, int64_t batch,
+                     int n, void* stream);
+
+/* ===========================================================================
+ * stream_mix_add: out = Phi x + Y              (v == NULL)
+ *                 out = Phi x + (v - Phi v)(v^T x) + Y   (v != NULL)
+ * x, Y, out share stream_dtype; Phi and v share param_dtype, which must be
+ * HC_DTYPE_F32 or equal to stream_dtype. fp32 accumulation.
+ * ======================================================================== */
+
+/* Replaces: hyperconnections/ops/stream_mix.py:57-86 (stream_mix_add) ->
+ * stream_mix_small_nb.py:75-132 (_stream_mix_fwd) and
+ * stream_mix_big_nb.py:74-146 (_stream_mix_fwd_big_nb). */
+int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y,
+                      const void* v, void* out, int64_t B, int n, int64_t D,
+                      int stream_dtype, int param_dtype, void* stream);
+
+/* Given G = dL/dout [B,n,D] (stream dtype):
+ *   grad_x   = Phi^T G (+ v beta^T)            [B,n,D] stream dtype (nullable)
+ *   grad_Phi = G x_eff^T                        [B,n,n] float32     (nullable)
+ *   grad_v   = rho - Phi^T rho + beta-part      [B,n]   float32     (nullable;
+ *              only with v != NULL)
+ * where, with v: alpha = v^T x, c = v - Phi v, beta = c^T G, x_eff = x - v alpha.
+ * grad_Y is G itself and is not produced here.
+ * Replaces: stream_mix_small_nb.py:341-391 (_StreamMixFn.backward) with its
+ * kernels :148-197 (_stream_mix_bwd_dx) and :213-263 (_stream_mix_bwd_dPhi). */
+int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x,
+                      const void* v, void* grad_x, float* grad_Phi,
+                      float* grad_v, int64_t B, int n, int64_t D,
+                      int stream_dtype, int param_dtype, void* stream);
+
+/* ===========================================================================
+ * Fused hyper-connection step with one backbone block (m = 1):
+ *   u      = sum_j alpha_j x_j                      (width-read)
+ *   x_out_i = sum_j H_ij x_j + beta_i f             (residual mix + depth-write)
+ * H, alpha, beta are float32; x, f, u, x_out share stream_dtype.
+ * Replaces the composition hyperconnections/cghc.py:410 (read einsum),
+ * :417 (write einsum) and :449 -> ops/stream_mix.py:57 (stream_mix_add),
+ * without materialising the write-out Y.
+ * ======================================================================== */
+int hc_fused_fwd(const void* x, const void* f, const float* H,
+                 const float* alpha, const float* beta, void* u, void* x_out,
+                 int64_t T, int n, int64_t D, int stream_dtype, void* stream);
+
+/* Given g_u = dL/du [T,D] and g_x = dL/dx_out [T,n,D]:
+ *   grad_x_j   = sum_i H_ij g_x_i + alpha_j g_u      [T,n,D] (nullable)
+ *   grad_f     = sum_i beta_i g_x_i                  [T,D]   (nullable)
+ *   grad_H_ij  = sum_d g_x_i x_j                     [T,n,n] float32 (nullable)
+ *   grad_alpha_j = sum_d g_u x_j                     [T,n]   float32 (nullable)
+ *   grad_beta_i  = sum_d g_x_i f                     [T,n]   float32 (nullable)
+ * Replaces the autograd backward of the same composition (einsum backward at
+ * cghc.py:410/:417 and stream_mix_small_nb.py:341-391). */
+int hc_fused_bwd(const void* g_u, const void* g_x, const void* x,
+                 const void* f, const float* H, const float* alpha,
+                 const float* beta, void* grad_x, void* grad_f,
+                 float* grad_H, float* grad_alpha, float* grad_beta,
+                 int64_t T, int n, int64_t D, int stream_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HCOPS_H */

@@ -1,0 +1,237 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE's own
+code (pjjajal/hyperconnections) on the CPU of this container.
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+What runs, all from the reference checkout, unmodified:
+  * expm_t18's Python body (hyperconnections/ops/expm.py:65-106) without its
+    torch.compile wrapper (the compiled form does not build on this CPU), with
+    autograd for the gradient -> expm_t18.npz;
+  * torch.linalg.matrix_exp, which CGHC calls (cghc.py:321) -> matrix_exp.npz;
+  * the reference's Triton stream-mix kernels and autograd Function
+    (ops/stream_mix_small_nb.py) under TRITON_INTERPRET=1 with a fixed BLOCK_D
+    (the autotuner needs a GPU) -> stream_mix_*.npz;
+  * CGHC's composition read einsum (cghc.py:410) -> write einsum (:417) ->
+    stream_mix_add (:449, the small-NB Function) in float32 on bf16-exact
+    inputs, forward and backward -> fused.npz.
+
+The reference imports timm only for trunc_normal_; a stub providing
+torch.nn.init.trunc_normal_ is written to a temporary directory and put on
+sys.path. Nothing else is patched. Inputs follow the reference tests' seeds
+(tests/test_ops.py:48-63) and the benchmark's structured-Phi families
+(benchmarks/stream_mix_bench.py:93-120).
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(path: str):
+    stub = tempfile.mkdtemp(prefix="timm_stub_")
+    os.makedirs(os.path.join(stub, "timm", "models"))
+    open(os.path.join(stub, "timm", "__init__.py"), "w").close()
+    open(os.path.join(stub, "timm", "models", "__init__.py"), "w").close()
+    with open(os.path.join(stub, "timm", "models", "layers.py"), "w") as fh:
+        fh.write("from torch.nn.init import trunc_normal_\n")
+    sys.path[:0] = [stub, path]
+    import hyperconnections.ops.expm as ref_expm
+    import hyperconnections.ops.stream_mix_small_nb as ref_small
+
+    return ref_expm, ref_small
+
+
+class _FixedBlock:
+    """Stands in for an autotuned Triton kernel: launches the inner JIT
+    function with one BLOCK_D (the interpreter cannot benchmark configs)."""
+
+    def __init__(self, autotuned, block_d):
+        self.fn = autotuned.fn
+        self.block_d = block_d
+
+    def __getitem__(self, grid):
+        meta = {"BLOCK_D": self.block_d}
+        g = grid(meta) if callable(grid) else grid
+
+        def launch(*args, **kwargs):
+            return self.fn[g](*args, BLOCK_D=self.block_d, **kwargs)
+
+        return launch
+
+
+def gen_expm(ref_expm, out):
+    body = ref_expm.expm_t18._torchdynamo_orig_callable
+    rec = {}
+    for n in (1, 2, 3, 4, 6, 8):
+        for kind in ("skew", "small", "scaled"):
+            g = torch.Generator().manual_seed(1000 + 10 * n + {"skew": 0, "small": 1, "scaled": 2}[kind])
+            B = 40
+            M = torch.randn(B, n, n, generator=g)
+            if kind == "skew":  # the config's distribution: 0.5 * (G - G^T) / 2
+                A = 0.5 * (M - M.mT) / 2
+            elif kind == "small":  # norms below theta_18: no scaling
+                A = 0.3 * M / n
+            else:  # norms above theta_18, mixed within the batch (s up to 3)
+                A = M * torch.linspace(0.5, 6.0, B).view(B, 1, 1) / n**0.5
+            Gr = torch.randn(B, n, n, generator=g)
+            A = A.float()
+            Ar = A.clone().requires_grad_(True)
+            E = body(Ar)
+            E.backward(Gr)
+            Am = A.clone().requires_grad_(True)
+            Em = torch.linalg.matrix_exp(Am)
+            Em.backward(Gr)
+            key = f"n{n}_{kind}"
+            rec[f"{key}_A"] = A.numpy()
+            rec[f"{key}_G"] = Gr.numpy()
+            rec[f"{key}_E"] = E.detach().numpy()
+            rec[f"{key}_dA"] = Ar.grad.numpy()
+            rec[f"{key}_Em"] = Em.detach().numpy()
+            rec[f"{key}_dAm"] = Am.grad.numpy()
+    np.savez_compressed(os.path.join(out, "expm.npz"), **rec)
+
+
+def _make_inputs(B, N, D, dtype, seed=0):  # reference tests/test_ops.py:48-57
+    torch.manual_seed(seed)
+    Phi = torch.randn(B, N, N, dtype=dtype)
+    x = torch.randn(B, N, D, dtype=dtype)
+    Y = torch.randn(B, N, D, dtype=dtype)
+    return Phi, x, Y
+
+
+def _make_v(B, N, dtype, seed=7):  # reference tests/test_ops.py:60-63
+    torch.manual_seed(seed)
+    return torch.nn.functional.normalize(torch.randn(B, N, dtype=dtype), dim=-1)
+
+
+def _structured_phi(kind, B, N, dtype):  # reference benchmarks/stream_mix_bench.py:93-111
+    if kind == "skew":
+        torch.manual_seed(1)
+        M = torch.randn(B, N, N, dtype=dtype) / N**0.5
+        return (M - M.mT).contiguous()
+    if kind == "psd":
+        torch.manual_seed(2)
+        R = torch.randn(B, N, N, dtype=dtype) / N**0.5
+        return (R @ R.mT).contiguous()
+    torch.manual_seed(3)
+    return torch.diag_embed(torch.randn(B, N, dtype=dtype)).contiguous()
+
+
+def gen_stream_mix(ref_small, out):
+    ref_small._stream_mix_fwd = _FixedBlock(ref_small._stream_mix_fwd, 32)
+    ref_small._stream_mix_bwd_dx = _FixedBlock(ref_small._stream_mix_bwd_dx, 32)
+    ref_small._stream_mix_bwd_dPhi = _FixedBlock(ref_small._stream_mix_bwd_dPhi, 64)
+    fn = ref_small.stream_mix_add_small_nb
+
+    cases = [  # (B, N, D, proj, phi kind) — the shapes of tests/test_ops.py
+        (1, 4, 64, False, "random"), (2, 8, 128, False, "random"), (4, 4, 256, False, "random"),
+        (3, 6, 48, False, "random"), (1, 4, 64, True, "random"), (2, 8, 128, True, "random"),
+        (3, 4, 48, True, "random"), (1, 4, 1, False, "random"), (1, 4, 7, False, "random"),
+        (1, 4, 33, False, "random"), (1, 4, 100, False, "random"), (3, 1, 64, False, "random"),
+        (2, 3, 40, True, "random"), (2, 5, 24, True, "random"), (1, 7, 16, True, "random"),
+        (2, 4, 64, True, "skew"), (2, 4, 64, True, "psd"), (2, 4, 64, True, "diag"),
+        (2, 2, 100, True, "random"),
+    ]
+    rec = {}
+    for ci, (B, N, D, proj, kind) in enumerate(cases):
+        Phi, x, Y = _make_inputs(B, N, D, torch.float32)
+        if kind != "random":
+            Phi = _structured_phi(kind, B, N, torch.float32)
+        v = _make_v(B, N, torch.float32) if proj else None
+        g = torch.Generator().manual_seed(500 + ci)
+        Gup = torch.randn(B, N, D, generator=g)
+        P = Phi.clone().requires_grad_(True)
+        X = x.clone().requires_grad_(True)
+        Yr = Y.clone().requires_grad_(True)
+        Vr = v.clone().requires_grad_(True) if proj else None
+        o = fn(P, X, Yr, Vr)
+        o.backward(Gup)
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([B, N, D, int(proj)])
+        rec[f"{key}_Phi"] = Phi.numpy()
+        rec[f"{key}_x"] = x.numpy()
+        rec[f"{key}_Y"] = Y.numpy()
+        rec[f"{key}_Gup"] = Gup.numpy()
+        rec[f"{key}_out"] = o.detach().numpy()
+        rec[f"{key}_gPhi"] = P.grad.numpy()
+        rec[f"{key}_gx"] = X.grad.numpy()
+        rec[f"{key}_gY"] = Yr.grad.numpy()
+        if proj:
+            rec[f"{key}_v"] = v.numpy()
+            rec[f"{key}_gv"] = Vr.grad.numpy()
+    np.savez_compressed(os.path.join(out, "stream_mix_f32.npz"), **rec)
+
+    # fp16 forward (reference tests/test_ops.py:106-112 compares fp16 output
+    # against the fp32 bmm of the same fp16 values)
+    rec16 = {}
+    for ci, (B, N, D) in enumerate([(2, 4, 128), (1, 8, 64), (2, 3, 40)]):
+        Phi, x, Y = _make_inputs(B, N, D, torch.float16)
+        o = fn(Phi, x, Y, None)
+        key = f"c{ci}"
+        rec16[f"{key}_Phi"] = Phi.numpy()
+        rec16[f"{key}_x"] = x.numpy()
+        rec16[f"{key}_Y"] = Y.numpy()
+        rec16[f"{key}_out"] = o.numpy()
+    np.savez_compressed(os.path.join(out, "stream_mix_f16.npz"), **rec16)
+
+
+def gen_fused(ref_small, out):
+    """CGHC composition (cghc.py:410, :417, :449) with m = 1, float32 math on
+    bf16-exact inputs drawn like the fused-step workload."""
+    fn = ref_small.stream_mix_add_small_nb
+    rec = {}
+    for ci, (T, n, D) in enumerate([(32, 4, 96), (24, 2, 64), (16, 3, 40), (16, 6, 48), (12, 8, 72), (8, 4, 100)]):
+        g = torch.Generator().manual_seed(2000 + ci)
+        bf = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).float()  # noqa: E731
+        x = bf(T, n, D)
+        f = bf(T, D)
+        S = torch.triu(0.5 * torch.randn(T, n, n, generator=g), 1)
+        H = torch.linalg.matrix_exp(S - S.mT)
+        alpha = torch.softmax(torch.randn(T, n, generator=g), -1)
+        beta = torch.softmax(torch.randn(T, n, generator=g), -1)
+        g_u = bf(T, D)
+        g_x = bf(T, n, D)
+        X, Fv, Hr, Ar, Br = (t.clone().requires_grad_(True) for t in (x, f, H, alpha, beta))
+        read_in = Ar[:, None, :]    # [T, m=1, n]
+        write_out = Br[:, :, None]  # [T, n, m=1]
+        u = torch.einsum("bmn,bnd->bmd", read_in, X)          # cghc.py:410
+        Y = torch.einsum("bnm,bmd->bnd", write_out, Fv[:, None, :])  # cghc.py:417
+        x_out = fn(Hr, X, Y, None)                              # cghc.py:449 -> :363
+        torch.autograd.backward([u, x_out], [g_u[:, None, :], g_x])
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([T, n, D])
+        for name, t in (("x", x), ("f", f), ("H", H), ("alpha", alpha), ("beta", beta), ("g_u", g_u),
+                        ("g_x", g_x), ("u", u[:, 0].detach()), ("x_out", x_out.detach()),
+                        ("grad_x", X.grad), ("grad_f", Fv.grad), ("grad_H", Hr.grad),
+                        ("grad_alpha", Ar.grad), ("grad_beta", Br.grad)):
+            rec[f"{key}_{name}"] = t.numpy()
+    np.savez_compressed(os.path.join(out, "fused.npz"), **rec)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--out", default=HERE)
+    args = ap.parse_args()
+    ref_expm, ref_small = _import_reference(args.reference)
+    gen_expm(ref_expm, args.out)
+    gen_stream_mix(ref_small, args.out)
+    gen_fused(ref_small, args.out)
+    for name in sorted(os.listdir(args.out)):
+        if name.endswith(".npz"):
+            print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+"""GPU parity tests of the batched matrix exponential (hc_expm_*).
+
+Expected values: the CPU oracle (oracle.expm: the T18 and Pade [7/7] schemes
+in float64, gradients by the block-triangular identity), outputs of the
+reference's own expm_t18 body and of torch.linalg.matrix_exp (golden
+fixtures), and scipy's float64 expm / expm_frechet. The parity bar is 1e-5
+relative Frobenius error per matrix in fp32.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import expm as oexpm
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+DEVICE = "cuda"
+TOL = 1e-5
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA not available")
+
+
+def ops():
+    from hyperconnections_b200 import ops as o
+
+    return o
+
+
+def fwd_bwd(fn, A, G):
+    At = A.detach().clone().requires_grad_(True)
+    E = fn(At)
+    E.backward(G)
+    return E.detach().cpu().numpy(), At.grad.cpu().numpy()
+
+
+def config_inputs(B, n, seed=0):
+    """The batched-expm workload: A = 0.5 (G - G^T) / 2 with G ~ N(0,1), then
+    an upstream gradient ~ N(0,1), drawn in that order from seed 0."""
+    g = torch.Generator().manual_seed(seed)
+    M = torch.randn(B, n, n, generator=g)
+    A = 0.5 * (M - M.mT) / 2
+    G = torch.randn(B, n, n, generator=g)
+    return A.to(DEVICE), G.to(DEVICE)
+
+
+EXPM = load_golden("expm.npz")
+KEYS = sorted({k.rsplit("_", 1)[0] for k in EXPM if k.endswith("_A")})
+
+
+@pytest.mark.parametrize("key", KEYS)
+def test_t18_global_matches_reference(key):
+    A = torch.from_numpy(EXPM[f"{key}_A"]).to(DEVICE)
+    G = torch.from_numpy(EXPM[f"{key}_G"]).to(DEVICE)
+    E, dA = fwd_bwd(ops().expm_t18, A, G)
+    An, Gn = EXPM[f"{key}_A"], EXPM[f"{key}_G"]
+    assert oexpm.rel_fro(E, oexpm.expm_t18(An)) < TOL
+    assert oexpm.rel_fro(dA, oexpm.expm_t18_grad(An, Gn)) < TOL
+    # and against the reference's own float32 outputs
+    assert oexpm.rel_fro(E, EXPM[f"{key}_E"]) < TOL
+    assert oexpm.rel_fro(dA, EXPM[f"{key}_dA"]) < TOL
+
+
+@pytest.mark.parametrize("key", KEYS)
+def test_t18_per_matrix(key):
+    A = torch.from_numpy(EXPM[f"{key}_A"]).to(DEVICE)
+    G = torch.from_numpy(EXPM[f"{key}_G"]).to(DEVICE)
+    E, dA = fwd_bwd(lambda a: ops().expm_t18(a, per_matrix_scaling=True), A, G)
+    An, Gn = EXPM[f"{key}_A"], EXPM[f"{key}_G"]
+    assert oexpm.rel_fro(E, oexpm.expm_t18(An, per_matrix=True)) < TOL
+    assert oexpm.rel_fro(dA, oexpm.expm_t18_grad(An, Gn, per_matrix=True)) < TOL
+
+
+@pytest.mark.parametrize("key", KEYS)
+def test_pade_matches_torch_matrix_exp(key):
+    A = torch.from_numpy(EXPM[f"{key}_A"]).to(DEVICE)
+    G = torch.from_numpy(EXPM[f"{key}_G"]).to(DEVICE)
+    E, dA = fwd_bwd(ops().matrix_exp, A, G)
+    An, Gn = EXPM[f"{key}_A"], EXPM[f"{key}_G"]
+    assert oexpm.rel_fro(E, oexpm.expm_pade(An)) < TOL
+    assert oexpm.rel_fro(dA, oexpm.expm_pade_grad(An, Gn)) < TOL
+    assert oexpm.rel_fro(E, EXPM[f"{key}_Em"]) < TOL
+    assert oexpm.rel_fro(dA, EXPM[f"{key}_dAm"]) < TOL
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_against_exact_exponential(n):
+    """Random matrices with norms spanning several scaling exponents (ragged
+    batch size) against scipy's float64 expm and expm_frechet."""
+    sl = pytest.importorskip("scipy.linalg")
+    B = 333
+    g = torch.Generator().manual_seed(n)
+    A = torch.randn(B, n, n, generator=g) * torch.logspace(-3, 1.2, B).view(B, 1, 1) / n**0.5
+    G = torch.randn(B, n, n, generator=g)
+    An, Gn = A.double().numpy(), G.double().numpy()
+    exact = np.stack([sl.expm(a) for a in An])
+    dexact = np.stack([sl.expm_frechet(a.T, gg, compute_expm=False) for a, gg in zip(An, Gn)])
+    for fn in (lambda a: ops().expm_t18(a, per_matrix_scaling=True), ops().matrix_exp):
+        E, dA = fwd_bwd(fn, A.to(DEVICE), G.to(DEVICE))
+        assert oexpm.rel_fro(E, exact) < TOL
+        assert oexpm.rel_fro(dA, dexact) < TOL
+
+
+def test_config_batch_full_size():
+    """The batched-expm workload (65,536 skew 4x4): exp of a skew matrix is
+    orthogonal; every matrix against the oracle, forward and gradient."""
+    A, G = config_inputs(65536, 4)
+    for fn, ofwd, ograd in ((ops().expm_t18, oexpm.expm_t18, oexpm.expm_t18_grad),
+                            (ops().matrix_exp, oexpm.expm_pade, oexpm.expm_pade_grad)):
+        E, dA = fwd_bwd(fn, A, G)
+        An, Gn = A.cpu().numpy(), G.cpu().numpy()
+        assert oexpm.rel_fro(E, ofwd(An)) < TOL
+        assert oexpm.rel_fro(dA, ograd(An, Gn)) < TOL
+        EEt = np.einsum("bij,bkj->bik", E.astype(np.float64), E.astype(np.float64))
+        assert np.abs(EEt - np.eye(4)).max() < 1e-5
+
+
+def test_zero_and_identity_and_shapes():
+    o = ops()
+    Z = torch.zeros(5, 3, 4, 4, device=DEVICE)
+    assert torch.equal(o.expm_t18(Z), torch.eye(4, device=DEVICE).expand(5, 3, 4, 4))
+    assert torch.equal(o.matrix_exp(Z), torch.eye(4, device=DEVICE).expand(5, 3, 4, 4))
+    assert o.expm_t18(torch.zeros(0, 4, 4, device=DEVICE)).shape == (0, 4, 4)
+    # single matrix, no batch dims
+    A = torch.tensor([[0.0, 1.0], [-1.0, 0.0]], device=DEVICE)
+    c, s = np.cos(1.0), np.sin(1.0)
+    assert np.abs(o.expm_t18(A).cpu().numpy() - np.array([[c, s], [-s, c]])).max() < 1e-6
+
+
+def test_large_norm_needs_more_than_eight_squarings():
+    """||A||_1 = 3000 > 3.01 * 2^8: the reference stops after 8 squarings
+    (expm.py:103-104); these kernels square s = 10 times."""
+    sl = pytest.importorskip("scipy.linalg")
+    A = torch.tensor([[[0.0, 1500.0], [-1500.0, 0.0]]])  # rotation by 1500 rad
+    exact = sl.expm(A[0].double().numpy())
+    for fn in (ops().expm_t18, ops().matrix_exp):
+        E = fn(A.to(DEVICE)).cpu().numpy()[0]
+        # fp32 conditioning of a 1500-rad rotation limits accuracy to ~1e-4
+        assert np.abs(E - exact).max() < 5e-4
+
+
+def test_errors():
+    o = ops()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        o.expm_t18(torch.zeros(2, 4, 4))
+    with pytest.raises(RuntimeError, match="n <= 8"):
+        o.expm_t18(torch.zeros(2, 9, 9, device=DEVICE))
+    with pytest.raises(ValueError):
+        o.matrix_exp(torch.zeros(2, 3, 4, device=DEVICE))

@@ -1,0 +1,161 @@
+"""GPU parity tests of the fused read + mix + write step (hc_fused_fwd/bwd).
+
+Expected values: the CPU oracle (oracle.stream_mix.fused_*), and golden
+fixtures produced by the reference's own composition (read einsum
+cghc.py:410 -> write einsum :417 -> stream_mix_add :449) in float32 on
+bf16-exact inputs. Tolerances: 1e-5 relative in fp32; 2e-2 absolute in bf16
+against an fp32-accumulated oracle of the same bf16 inputs (parameter
+gradients, which are fp32 sums over D, are held to 1e-5 relative).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import stream_mix as omix
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+DEVICE = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA not available")
+
+
+def fused(*a):
+    from hyperconnections_b200.ops import stream_mix_fused
+
+    return stream_mix_fused(*a)
+
+
+def np64(t):
+    return t.detach().double().cpu().numpy()
+
+
+def workload(T, n, D, dtype, seed=0):
+    """The fused-step workload's distributions, drawn in a fixed order from one
+    CPU generator: x, f ~ N(0,1); H = expm(S - S^T) with S the strict upper
+    triangle of 0.5 * N(0,1) (skew-symmetric, off-diagonal entries exactly
+    N(0, 0.5^2)); alpha, beta = softmax of N(0,1) logits; upstream gradients
+    g_u, g_x ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, n, D, generator=g).to(dtype)
+    f = torch.randn(T, D, generator=g).to(dtype)
+    S = torch.triu(0.5 * torch.randn(T, n, n, generator=g), 1)
+    H = torch.linalg.matrix_exp(S - S.mT)
+    alpha = torch.softmax(torch.randn(T, n, generator=g), -1)
+    beta = torch.softmax(torch.randn(T, n, generator=g), -1)
+    g_u = torch.randn(T, D, generator=g).to(dtype)
+    g_x = torch.randn(T, n, D, generator=g).to(dtype)
+    return [t.to(DEVICE) for t in (x, f, H, alpha, beta, g_u, g_x)]
+
+
+def run(x, f, H, alpha, beta, g_u, g_x):
+    ts = [t.detach().clone().requires_grad_(True) for t in (x, f, H, alpha, beta)]
+    u, x_out = fused(*ts)
+    torch.autograd.backward([u, x_out], [g_u, g_x])
+    return u, x_out, [t.grad for t in ts]
+
+
+def check(u, x_out, grads, inputs, stream_tol, rel):
+    x, f, H, alpha, beta, g_u, g_x = [np64(t) for t in inputs]
+    ru, rx = omix.fused_fwd(x, f, H, alpha, beta)
+    rg = omix.fused_bwd(g_u, g_x, x, f, H, alpha, beta)
+
+    def close(got, ref, what, absolute):
+        err = np.abs(np64(got) - ref).max() if ref.size else 0.0
+        bound = absolute if not rel else absolute * max(1.0, np.abs(ref).max())
+        assert err <= bound, f"{what}: max err {err:.3e} > {bound:.3e}"
+
+    close(u, ru, "u", stream_tol)
+    close(x_out, rx, "x_out", stream_tol)
+    close(grads[0], rg[0], "grad_x", stream_tol)
+    close(grads[1], rg[1], "grad_f", stream_tol)
+    for got, ref, name in zip(grads[2:], rg[2:], ("grad_H", "grad_alpha", "grad_beta")):
+        err = np.abs(np64(got) - ref).max()
+        assert err <= 1e-5 * max(1.0, np.abs(ref).max()), f"{name}: {err:.3e}"
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("D", [768, 64, 100, 7])
+def test_fused_fp32(n, D):
+    inputs = workload(37, n, D, torch.float32, seed=n * 100 + D)
+    u, x_out, grads = run(*inputs)
+    check(u, x_out, grads, inputs, 1e-5, rel=True)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,D", [(4, 768), (2, 512), (3, 1024), (6, 2048), (8, 4096), (4, 100), (5, 24)])
+def test_fused_half(dtype, n, D):
+    inputs = workload(29, n, D, dtype, seed=7 * n + D)
+    u, x_out, grads = run(*inputs)
+    assert u.dtype == dtype and x_out.dtype == dtype and grads[0].dtype == dtype
+    assert grads[2].dtype == torch.float32
+    check(u, x_out, grads, inputs, 2e-2, rel=False)
+
+
+FUSED = load_golden("fused.npz")
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in FUSED}))
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_golden_reference_composition(case, dtype):
+    g = lambda name: torch.from_numpy(FUSED[f"{case}_{name}"]).to(DEVICE)  # noqa: E731
+    x, f, g_u, g_x = (g(k).to(dtype) for k in ("x", "f", "g_u", "g_x"))  # bf16-exact values
+    H, alpha, beta = g("H"), g("alpha"), g("beta")
+    u, x_out, grads = run(x, f, H, alpha, beta, g_u, g_x)
+    ref = lambda name: FUSED[f"{case}_{name}"].astype(np.float64)  # noqa: E731
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    for got, name in ((u, "u"), (x_out, "x_out"), (grads[0], "grad_x"), (grads[1], "grad_f")):
+        r = ref(name)
+        bound = tol * max(1.0, np.abs(r).max()) if dtype == torch.float32 else tol
+        assert np.abs(np64(got) - r).max() <= bound, name
+    for got, name in zip(grads[2:], ("grad_H", "grad_alpha", "grad_beta")):
+        r = ref(name)
+        assert np.abs(np64(got) - r).max() <= 1e-5 * max(1.0, np.abs(r).max()), name
+
+
+def test_fused_full_size_workload():
+    """The full fused-step workload (x [16,1024,4,768] bf16): every output
+    against the oracle, plus leading-dimension handling."""
+    T, n, D = 16 * 1024, 4, 768
+    x, f, H, alpha, beta, g_u, g_x = workload(T, n, D, torch.bfloat16, seed=0)
+    shp = lambda t: t.view(16, 1024, *t.shape[1:])  # noqa: E731
+    ins = [shp(t) for t in (x, f, H, alpha, beta)]
+    ts = [t.detach().clone().requires_grad_(True) for t in ins]
+    u, x_out = fused(*ts)
+    assert u.shape == (16, 1024, D) and x_out.shape == (16, 1024, n, D)
+    torch.autograd.backward([u, x_out], [shp(g_u), shp(g_x)])
+    grads = [t.grad.reshape(T, *t.shape[2:]) for t in ts]
+    check(u.reshape(T, D), x_out.reshape(T, n, D), grads, (x, f, H, alpha, beta, g_u, g_x), 2e-2, rel=False)
+
+
+def test_fused_linearity_and_identity():
+    """Size-independent properties: with H = I, alpha = e_0, beta = 0 the step
+    returns (x_0, x); the forward is linear in (x, f)."""
+    T, n, D = 4096, 4, 768
+    x, f, H, alpha, beta, _, _ = workload(T, n, D, torch.float32, seed=3)
+    eye = torch.eye(n, device=DEVICE).expand(T, n, n).contiguous()
+    e0 = torch.zeros(T, n, device=DEVICE)
+    e0[:, 0] = 1
+    u, xo = fused(x, f, eye, e0, torch.zeros_like(beta))
+    assert torch.equal(u, x[:, 0]) and torch.equal(xo, x)
+    u1, x1 = fused(x, f, H, alpha, beta)
+    u2, x2 = fused(2 * x, 2 * f, H, alpha, beta)
+    assert torch.allclose(u2, 2 * u1, rtol=0, atol=0) and torch.allclose(x2, 2 * x1, rtol=0, atol=0)
+
+
+def test_fused_errors():
+    x, f, H, alpha, beta, _, _ = workload(4, 4, 64, torch.float32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused(x.cpu(), f, H, alpha, beta)
+    x9 = torch.randn(4, 9, 64, device=DEVICE)
+    with pytest.raises(RuntimeError, match="n <= 8"):
+        fused(x9, f, torch.randn(4, 9, 9, device=DEVICE), torch.randn(4, 9, device=DEVICE),
+              torch.randn(4, 9, device=DEVICE))
+    with pytest.raises(AssertionError):
+        fused(x, f[:, :32], H, alpha, beta)

@@ -1,0 +1,90 @@
+"""Pins the CPU oracle against outputs of the reference's own code
+(tests/golden/*.npz, made by tests/golden/make_golden.py). CPU only."""
+
+import numpy as np
+import pytest
+
+from oracle import expm as oexpm
+from oracle import stream_mix as omix
+from tests.conftest import load_golden
+
+EXPM = load_golden("expm.npz")
+MIX32 = load_golden("stream_mix_f32.npz")
+MIX16 = load_golden("stream_mix_f16.npz")
+FUSED = load_golden("fused.npz")
+
+EXPM_KEYS = sorted({k.rsplit("_", 1)[0] for k in EXPM if k.endswith("_A")})
+
+
+@pytest.mark.parametrize("key", EXPM_KEYS)
+def test_oracle_expm_t18_matches_reference(key):
+    A, G = EXPM[f"{key}_A"], EXPM[f"{key}_G"]
+    E = oexpm.expm_t18(A)
+    dA = oexpm.expm_t18_grad(A, G)
+    # reference runs the same scheme in float32; the oracle in float64
+    assert oexpm.rel_fro(E, EXPM[f"{key}_E"]) < 1e-5
+    assert oexpm.rel_fro(dA, EXPM[f"{key}_dA"]) < 1e-5
+
+
+@pytest.mark.parametrize("key", EXPM_KEYS)
+def test_oracle_pade_matches_torch_matrix_exp(key):
+    A, G = EXPM[f"{key}_A"], EXPM[f"{key}_G"]
+    assert oexpm.rel_fro(oexpm.expm_pade(A), EXPM[f"{key}_Em"]) < 1e-5
+    assert oexpm.rel_fro(oexpm.expm_pade_grad(A, G), EXPM[f"{key}_dAm"]) < 1e-5
+
+
+@pytest.mark.parametrize("key", EXPM_KEYS)
+def test_oracle_approximants_match_exact_exponential(key):
+    """T18 and Pade [7/7] agree with scipy's float64 expm / expm_frechet to
+    far below the 1e-5 parity tolerance."""
+    scipy_linalg = pytest.importorskip("scipy.linalg")
+    A, G = EXPM[f"{key}_A"].astype(np.float64), EXPM[f"{key}_G"].astype(np.float64)
+    exact = np.stack([scipy_linalg.expm(a) for a in A])
+    dexact = np.stack([scipy_linalg.expm_frechet(a.T, g, compute_expm=False) for a, g in zip(A, G)])
+    assert oexpm.rel_fro(oexpm.expm_t18(A), exact) < 1e-6
+    assert oexpm.rel_fro(oexpm.expm_pade(A), exact) < 1e-6
+    assert oexpm.rel_fro(oexpm.expm_t18_grad(A, G), dexact) < 1e-6
+    assert oexpm.rel_fro(oexpm.expm_pade_grad(A, G), dexact) < 1e-6
+
+
+def test_scaling_exponent_matches_reference_rule():
+    # s = ceil(log2(norm / 3.01)) clamped at 0 (reference expm.py:81-85)
+    norms = np.array([0.0, 1.0, 3.01, 3.02, 6.02, 6.03, 770.0, 1e6], dtype=np.float32)
+    want = [0, 0, 0, 1, 1, 2, 8, 19]
+    assert oexpm.scaling_exponent(norms, oexpm.THETA_18).tolist() == want
+
+
+MIX_CASES = sorted({k.split("_")[0] for k in MIX32})
+
+
+@pytest.mark.parametrize("case", MIX_CASES)
+def test_oracle_stream_mix_matches_reference_triton(case):
+    g = lambda name: MIX32[f"{case}_{name}"]  # noqa: E731
+    proj = bool(g("meta")[3])
+    v = g("v") if proj else None
+    out = omix.stream_mix_fwd(g("Phi"), g("x"), g("Y"), v)
+    np.testing.assert_allclose(out, g("out"), rtol=1e-5, atol=1e-5)
+    gPhi, gx, gY, gv = omix.stream_mix_bwd(g("Gup"), g("Phi"), g("x"), v)
+    np.testing.assert_allclose(gx, g("gx"), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(gPhi, g("gPhi"), rtol=1e-4, atol=1e-4)
+    np.testing.assert_array_equal(gY, g("gY"))
+    if proj:
+        np.testing.assert_allclose(gv, g("gv"), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in MIX16}))
+def test_oracle_stream_mix_fp16_matches_reference(case):
+    g = lambda name: MIX16[f"{case}_{name}"]  # noqa: E731
+    out = omix.stream_mix_fwd(g("Phi"), g("x"), g("Y"))
+    np.testing.assert_allclose(out, g("out").astype(np.float64), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in FUSED}))
+def test_oracle_fused_matches_reference_composition(case):
+    g = lambda name: FUSED[f"{case}_{name}"]  # noqa: E731
+    u, x_out = omix.fused_fwd(g("x"), g("f"), g("H"), g("alpha"), g("beta"))
+    np.testing.assert_allclose(u, g("u"), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(x_out, g("x_out"), rtol=1e-5, atol=1e-5)
+    grads = omix.fused_bwd(g("g_u"), g("g_x"), g("x"), g("f"), g("H"), g("alpha"), g("beta"))
+    for name, got in zip(("grad_x", "grad_f", "grad_H", "grad_alpha", "grad_beta"), grads):
+        np.testing.assert_allclose(got, g(name), rtol=1e-4, atol=1e-4, err_msg=name)
