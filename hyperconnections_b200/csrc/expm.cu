@@ -590,7 +590,8 @@ dim3 expm_grid(int64_t batch, int n) {
 int check(const void* a, const void* b, int64_t batch, int n) {
   if (batch < 0) return HC_ERR_BAD_SIZE;
   if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
-  if (batch > (int64_t(1) << 40)) return HC_ERR_BAD_SIZE;
+  // batch * 8 lanes / 256 threads per CTA must stay below 2^31 CTAs
+  if (batch > (int64_t(1) << 34)) return HC_ERR_BAD_SIZE;
   if (batch == 0) return HC_OK;
   if (!a || !b) return HC_ERR_NULL_POINTER;
   if (!aligned4(a) || !aligned4(b)) return HC_ERR_ALIGNMENT;

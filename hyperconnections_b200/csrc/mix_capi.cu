@@ -10,6 +10,7 @@ namespace hc {
 namespace {
 
 constexpr int64_t kMaxD = int64_t(1) << 24;
+constexpr int64_t kMaxTokens = (int64_t(1) << 31) - 1;
 
 int check_dtypes(int sdt, int pdt) {
   if (dtype_size(sdt) == 0 || dtype_size(pdt) == 0) return HC_ERR_DTYPE;
@@ -18,7 +19,8 @@ int check_dtypes(int sdt, int pdt) {
 }
 
 int check_sizes(int64_t T, int n, int64_t D) {
-  if (T < 0 || D < 0 || D > kMaxD) return HC_ERR_BAD_SIZE;
+  // one CTA row per token: the grid must stay within 2^31 - 1 CTAs
+  if (T < 0 || T > kMaxTokens || D < 0 || D > kMaxD) return HC_ERR_BAD_SIZE;
   if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
   return HC_OK;
 }
