@@ -3,9 +3,10 @@
 Expected values: the CPU oracle (oracle.stream_mix.fused_*), and golden
 fixtures produced by the reference's own composition (read einsum
 cghc.py:410 -> write einsum :417 -> stream_mix_add :449) in float32 on
-bf16-exact inputs. Tolerances: 1e-5 relative in fp32; 2e-2 absolute in bf16
-against an fp32-accumulated oracle of the same bf16 inputs (parameter
-gradients, which are fp32 sums over D, are held to 1e-5 relative).
+bf16-exact inputs. Tolerances: 1e-5 relative in fp32; in bf16, 2e-2 absolute
+plus 2^-7 |ref| (the output rounding of values >= 8, whose bf16 half-ulp alone
+exceeds 2e-2) against an fp32-accumulated oracle of the same bf16 inputs.
+Parameter gradients, fp32 sums over D, are held to 1e-5 relative.
 """
 
 import numpy as np
@@ -66,10 +67,14 @@ def check(u, x_out, grads, inputs, stream_tol, rel):
     ru, rx = omix.fused_fwd(x, f, H, alpha, beta)
     rg = omix.fused_bwd(g_u, g_x, x, f, H, alpha, beta)
 
-    def close(got, ref, what, absolute):
-        err = np.abs(np64(got) - ref).max() if ref.size else 0.0
-        bound = absolute if not rel else absolute * max(1.0, np.abs(ref).max())
-        assert err <= bound, f"{what}: max err {err:.3e} > {bound:.3e}"
+    def close(got, ref, what, tol):
+        if rel:  # fp32: tol relative to the largest magnitude
+            err = np.abs(np64(got) - ref).max() if ref.size else 0.0
+            bound = tol * max(1.0, np.abs(ref).max() if ref.size else 0.0)
+            assert err <= bound, f"{what}: max err {err:.3e} > {bound:.3e}"
+        else:  # half: tol absolute, plus 2^-7 |ref| for the output rounding of large values
+            excess = np.abs(np64(got) - ref) - (tol + 2.0**-7 * np.abs(ref))
+            assert excess.max(initial=-1.0) <= 0, f"{what}: exceeds bound by {excess.max():.3e}"
 
     close(u, ru, "u", stream_tol)
     close(x_out, rx, "x_out", stream_tol)
@@ -109,11 +114,12 @@ def test_golden_reference_composition(case, dtype):
     H, alpha, beta = g("H"), g("alpha"), g("beta")
     u, x_out, grads = run(x, f, H, alpha, beta, g_u, g_x)
     ref = lambda name: FUSED[f"{case}_{name}"].astype(np.float64)  # noqa: E731
-    tol = 1e-5 if dtype == torch.float32 else 2e-2
     for got, name in ((u, "u"), (x_out, "x_out"), (grads[0], "grad_x"), (grads[1], "grad_f")):
         r = ref(name)
-        bound = tol * max(1.0, np.abs(r).max()) if dtype == torch.float32 else tol
-        assert np.abs(np64(got) - r).max() <= bound, name
+        if dtype == torch.float32:
+            assert np.abs(np64(got) - r).max() <= 1e-5 * max(1.0, np.abs(r).max()), name
+        else:
+            assert (np.abs(np64(got) - r) - (2e-2 + 2.0**-7 * np.abs(r))).max() <= 0, name
     for got, name in zip(grads[2:], ("grad_H", "grad_alpha", "grad_beta")):
         r = ref(name)
         assert np.abs(np64(got) - r).max() <= 1e-5 * max(1.0, np.abs(r).max()), name
