@@ -35,6 +35,7 @@ _vp = ctypes.c_void_p
 _SIGNATURES = {
     "hc_error_string": (ctypes.c_char_p, [_c_int]),
     "hc_abi_version": (_c_int, []),
+    "hc_wait_timeouts": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
     "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
     "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_t18_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
@@ -116,3 +117,11 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 def stream_of(t: torch.Tensor) -> int:
     """Raw cudaStream_t of torch's current stream on the tensor's device."""
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def wait_timeouts(reset: bool = False) -> int:
+    """Number of bounded kernel waits that gave up on the current device
+    (synchronises the device)."""
+    count = ctypes.c_uint(0)
+    check(lib().hc_wait_timeouts(ctypes.byref(count), 1 if reset else 0), "hc_wait_timeouts")
+    return int(count.value)

@@ -53,6 +53,14 @@ const char* hc_error_string(int code);
 /* Library ABI version; bumped whenever a signature below changes. */
 int hc_abi_version(void);
 
+/* Diagnostics: synchronises the current device, then stores in *count how
+ * many bounded pipeline waits inside the stream-mixing kernels gave up since
+ * the last reset (0 in a healthy run; a kernel that gives up leaves its
+ * outputs incomplete and returns instead of spinning). reset != 0 clears the
+ * counters. No reference counterpart (the reference's Triton kernels have no
+ * such waits). */
+int hc_wait_timeouts(unsigned int* count, int reset);
+
 /* ===========================================================================
  * Batched matrix exponential, n <= 8, float32.
  * ======================================================================== */
