@@ -36,6 +36,7 @@ _SIGNATURES = {
     "hc_error_string": (ctypes.c_char_p, [_c_int]),
     "hc_abi_version": (_c_int, []),
     "hc_wait_timeouts": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
+    "hc_set_mix_tuning": (_c_int, [_c_int, _c_int, _c_int]),
     "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
     "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_t18_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),

@@ -4,7 +4,7 @@
 // dtype codes, NULL pointers and alignment. The 16-byte vector path is taken
 // when D is a multiple of the chunk width and every stream base pointer is
 // 16-byte aligned; otherwise the element-wise path of the same kernels runs.
-#include "mix_tma.cuh"
+#include "mix_warp.cuh"
 
 namespace hc {
 namespace {
@@ -60,30 +60,30 @@ int sm_count() {
   return n;
 }
 
-int run_fwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const TmaGeometry& g, const MixFwdArgs& a,
+int run_fwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const WarpGeometry& g, const MixFwdArgs& a,
                 cudaStream_t s) {
   switch (sdt) {
-    case HC_DTYPE_F32: return mix_fwd_tma_f32(fused, proj, pf32, n, g, a, s);
-    case HC_DTYPE_F16: return mix_fwd_tma_f16(fused, proj, pf32, n, g, a, s);
-    case HC_DTYPE_BF16: return mix_fwd_tma_bf16(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_F32: return mix_fwd_warp_f32(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_F16: return mix_fwd_warp_f16(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_BF16: return mix_fwd_warp_bf16(fused, proj, pf32, n, g, a, s);
   }
   return HC_ERR_DTYPE;
 }
 
-int run_bwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const TmaGeometry& g, const MixBwdArgs& a,
+int run_bwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const WarpGeometry& g, const MixBwdArgs& a,
                 cudaStream_t s) {
   switch (sdt) {
-    case HC_DTYPE_F32: return mix_bwd_tma_f32(fused, proj, pf32, n, g, a, s);
-    case HC_DTYPE_F16: return mix_bwd_tma_f16(fused, proj, pf32, n, g, a, s);
-    case HC_DTYPE_BF16: return mix_bwd_tma_bf16(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_F32: return mix_bwd_warp_f32(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_F16: return mix_bwd_warp_f16(fused, proj, pf32, n, g, a, s);
+    case HC_DTYPE_BF16: return mix_bwd_warp_bf16(fused, proj, pf32, n, g, a, s);
   }
   return HC_ERR_DTYPE;
 }
 
-// The pipelined kernels need 16-byte chunks (D % chunk == 0) and 16-byte
-// aligned stream bases, and write every output with 16-byte stores.
-bool use_tma(bool vec, TmaGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int sdt) {
-  return vec && tma_geometry(geo, bwd, fused, n, T, D, dtype_size(sdt), sm_count());
+// The pipelined kernels need D % (16 B / element) == 0 (bulk copies move
+// multiples of 16 bytes) and 16-byte aligned stream bases.
+bool use_tma(bool vec, WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int sdt) {
+  return vec && warp_geometry(geo, bwd, fused, n, T, D, dtype_size(sdt), sm_count());
 }
 
 }  // namespace
@@ -107,7 +107,7 @@ extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, 
   MixFwdArgs a{};
   a.x = x; a.src = Y; a.phi = Phi; a.v = v; a.out = out;
   a.T = B; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
-  TmaGeometry geo;
+  WarpGeometry geo;
   if (use_tma(vec, geo, false, false, n, B, D, stream_dtype))
     return run_fwd_tma(stream_dtype, false, v != nullptr, param_dtype == HC_DTYPE_F32, n, geo, a,
                        static_cast<cudaStream_t>(stream));
@@ -135,7 +135,7 @@ extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, 
   a.g = G; a.x = x; a.phi = Phi; a.v = v;
   a.grad_x = D > 0 ? grad_x : nullptr; a.grad_phi = grad_Phi; a.grad_v = grad_v;
   a.T = B; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
-  TmaGeometry geo;
+  WarpGeometry geo;
   if (use_tma(vec, geo, true, false, n, B, D, stream_dtype))
     return run_bwd_tma(stream_dtype, false, v != nullptr, param_dtype == HC_DTYPE_F32, n, geo, a,
                        static_cast<cudaStream_t>(stream));
@@ -159,7 +159,7 @@ extern "C" int hc_fused_fwd(const void* x, const void* f, const float* H, const 
   MixFwdArgs a{};
   a.x = x; a.src = f; a.phi = H; a.alpha = alpha; a.beta = beta; a.out = x_out; a.u = u;
   a.T = T; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
-  TmaGeometry geo;
+  WarpGeometry geo;
   if (use_tma(vec, geo, false, true, n, T, D, stream_dtype))
     return run_fwd_tma(stream_dtype, true, false, true, n, geo, a, static_cast<cudaStream_t>(stream));
   return run_fwd(stream_dtype, true, false, vec, true, n, g, a, static_cast<cudaStream_t>(stream));
@@ -188,7 +188,7 @@ extern "C" int hc_fused_bwd(const void* g_u, const void* g_x, const void* x, con
   a.grad_x = D > 0 ? grad_x : nullptr; a.grad_f = D > 0 ? grad_f : nullptr;
   a.grad_phi = grad_H; a.grad_alpha = grad_alpha; a.grad_beta = grad_beta;
   a.T = T; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
-  TmaGeometry geo;
+  WarpGeometry geo;
   if (use_tma(vec, geo, true, true, n, T, D, stream_dtype))
     return run_bwd_tma(stream_dtype, true, false, true, n, geo, a, static_cast<cudaStream_t>(stream));
   return run_bwd(stream_dtype, true, false, vec, true, n, g, a, static_cast<cudaStream_t>(stream));
@@ -197,7 +197,21 @@ extern "C" int hc_fused_bwd(const void* g_u, const void* g_x, const void* x, con
 extern "C" int hc_wait_timeouts(unsigned int* count, int reset) {
   if (!count) return HC_ERR_NULL_POINTER;
   if (cudaDeviceSynchronize() != cudaSuccess) return HC_ERR_LAUNCH;
-  *count = mix_tma_take_timeouts_f32(reset != 0) + mix_tma_take_timeouts_f16(reset != 0) +
-           mix_tma_take_timeouts_bf16(reset != 0);
+  *count = mix_warp_take_timeouts_f32(reset != 0) + mix_warp_take_timeouts_f16(reset != 0) +
+           mix_warp_take_timeouts_bf16(reset != 0);
+  return HC_OK;
+}
+
+namespace hc {
+WarpTuning& warp_tuning() {
+  static WarpTuning t{0, 0, 0};
+  return t;
+}
+}  // namespace hc
+
+extern "C" int hc_set_mix_tuning(int stage_bytes, int stages, int warps) {
+  if (stage_bytes < 0 || stages < 0 || stages > kWarpMaxStages || warps < 0 || warps > kWarpMaxWarps)
+    return HC_ERR_BAD_SIZE;
+  hc::warp_tuning() = hc::WarpTuning{stage_bytes, stages, warps};
   return HC_OK;
 }

@@ -2,7 +2,7 @@
 // Included by mix_f32.cu / mix_f16.cu / mix_bf16.cu with HC_T (the element
 // type) and HC_SUFFIX (the entry-point suffix) defined, so the three dtypes
 // compile as separate translation units in parallel.
-#include "mix_tma.cuh"
+#include "mix_warp.cuh"
 
 #define HC_CAT2(a, b) a##b
 #define HC_CAT(a, b) HC_CAT2(a, b)
@@ -29,42 +29,42 @@ int add_bwd(bool proj, bool vec, int n, const MixGeometry& g, const MixBwdArgs& 
 }
 
 template <typename T, typename P>
-int add_fwd_tma(bool proj, int n, const TmaGeometry& g, const MixFwdArgs& a, cudaStream_t s) {
-  return proj ? launch_mix_fwd_tma<T, P, false, true>(n, g, a, s) : launch_mix_fwd_tma<T, P, false, false>(n, g, a, s);
+int add_fwd_warp(bool proj, int n, const WarpGeometry& g, const MixFwdArgs& a, cudaStream_t s) {
+  return proj ? launch_mix_fwd_warp<T, P, false, true>(n, g, a, s) : launch_mix_fwd_warp<T, P, false, false>(n, g, a, s);
 }
 
 template <typename T, typename P>
-int add_bwd_tma(bool proj, int n, const TmaGeometry& g, const MixBwdArgs& a, cudaStream_t s) {
-  return proj ? launch_mix_bwd_tma<T, P, false, true>(n, g, a, s) : launch_mix_bwd_tma<T, P, false, false>(n, g, a, s);
+int add_bwd_warp(bool proj, int n, const WarpGeometry& g, const MixBwdArgs& a, cudaStream_t s) {
+  return proj ? launch_mix_bwd_warp<T, P, false, true>(n, g, a, s) : launch_mix_bwd_warp<T, P, false, false>(n, g, a, s);
 }
 
 }  // namespace
 
-int HC_CAT(mix_fwd_tma_, HC_SUFFIX)(bool fused, bool proj, bool param_is_f32, int n, const TmaGeometry& g,
+int HC_CAT(mix_fwd_warp_, HC_SUFFIX)(bool fused, bool proj, bool param_is_f32, int n, const WarpGeometry& g,
                                    const MixFwdArgs& a, cudaStream_t s) {
   using T = HC_T;
-  if (fused) return launch_mix_fwd_tma<T, float, true, false>(n, g, a, s);
+  if (fused) return launch_mix_fwd_warp<T, float, true, false>(n, g, a, s);
 #if HC_T_IS_F32
   (void)param_is_f32;
-  return add_fwd_tma<T, float>(proj, n, g, a, s);
+  return add_fwd_warp<T, float>(proj, n, g, a, s);
 #else
-  return param_is_f32 ? add_fwd_tma<T, float>(proj, n, g, a, s) : add_fwd_tma<T, T>(proj, n, g, a, s);
+  return param_is_f32 ? add_fwd_warp<T, float>(proj, n, g, a, s) : add_fwd_warp<T, T>(proj, n, g, a, s);
 #endif
 }
 
-int HC_CAT(mix_bwd_tma_, HC_SUFFIX)(bool fused, bool proj, bool param_is_f32, int n, const TmaGeometry& g,
+int HC_CAT(mix_bwd_warp_, HC_SUFFIX)(bool fused, bool proj, bool param_is_f32, int n, const WarpGeometry& g,
                                    const MixBwdArgs& a, cudaStream_t s) {
   using T = HC_T;
-  if (fused) return launch_mix_bwd_tma<T, float, true, false>(n, g, a, s);
+  if (fused) return launch_mix_bwd_warp<T, float, true, false>(n, g, a, s);
 #if HC_T_IS_F32
   (void)param_is_f32;
-  return add_bwd_tma<T, float>(proj, n, g, a, s);
+  return add_bwd_warp<T, float>(proj, n, g, a, s);
 #else
-  return param_is_f32 ? add_bwd_tma<T, float>(proj, n, g, a, s) : add_bwd_tma<T, T>(proj, n, g, a, s);
+  return param_is_f32 ? add_bwd_warp<T, float>(proj, n, g, a, s) : add_bwd_warp<T, T>(proj, n, g, a, s);
 #endif
 }
 
-unsigned int HC_CAT(mix_tma_take_timeouts_, HC_SUFFIX)(bool reset) {
+unsigned int HC_CAT(mix_warp_take_timeouts_, HC_SUFFIX)(bool reset) {
   unsigned int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_mix_wait_timeouts, sizeof(v)) != cudaSuccess) {
     cudaGetLastError();

@@ -61,6 +61,13 @@ int hc_abi_version(void);
  * such waits). */
 int hc_wait_timeouts(unsigned int* count, int reset);
 
+/* Performance tuning of the pipelined stream-mixing kernels, process-wide:
+ * target bytes of one pipeline stage, stages per warp and warps per CTA; 0
+ * keeps the automatic choice for that knob. Results do not depend on these
+ * settings. No reference counterpart (the reference autotunes its Triton
+ * block sizes, ops/stream_mix_small_nb.py:52-67). */
+int hc_set_mix_tuning(int stage_bytes, int stages, int warps);
+
 /* ===========================================================================
  * Batched matrix exponential, n <= 8, float32.
  * ======================================================================== */
