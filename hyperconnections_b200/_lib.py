@@ -39,6 +39,7 @@ _SIGNATURES = {
     "hc_set_mix_tuning": (_c_int, [_c_int, _c_int, _c_int]),
     "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
     "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
+    "hc_expm_t18_fwd_noalloc": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_t18_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_pade_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_pade_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _vp]),

@@ -33,6 +33,8 @@
 // of the Matrix Exponential, with an Application to Condition Number
 // Estimation", SIAM J. Matrix Anal. Appl. 30 (2009)). The scaling exponent is
 // the forward's (from ||A||_1, not ||A^T||_1).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace hc {
@@ -694,6 +696,70 @@ extern "C" int hc_expm_pade_bwd(const float* A, const float* G, float* dA, int64
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid = expm_grid(batch, n);
 #define L(NN) expm_pade_bwd_kernel<NN><<<grid, kExpmThreads, 0, st>>>(A, G, dA, batch)
+  HC_EXPM_SWITCH(n, L)
+#undef L
+  return launch_status();
+}
+
+// ------------------------------------------------------------ no-allocation variant
+// Some callers cannot allocate device memory at all: a plugin or FFI caller
+// that only ever receives pointers from a host framework which owns every
+// byte of device memory, or a latency-critical loop that must not call
+// cudaMalloc because it can synchronise the whole device. For them,
+// hc_expm_t18_fwd_noalloc keeps the global-scaling scratch (one partial
+// maximum of ||A||_1 per CTA of the norm kernel) in this fixed array instead
+// of a caller buffer. Every GPU that loads the library holds these 4 KB until
+// the process exits.
+namespace hc {
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+static __device__ __align__(256) float g_t18_noalloc_partials[kMaxNormParts];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_dev_ptr[kNoallocMaxDevices] = {};
+
+// Device address of the array on the current device, looked up once per
+// device (the array's name in host code is only a host-side stand-in).
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return HC_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kNoallocMaxDevices) return HC_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_dev_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_t18_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return HC_ERR_LAUNCH;
+    }
+    g_noalloc_dev_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_dev_ptr[dev];
+  return HC_OK;
+}
+
+}  // namespace
+}  // namespace hc
+
+extern "C" int hc_expm_t18_fwd_noalloc(const float* A, float* E, int64_t batch, int n, void* stream) {
+  int rc = check(A, E, batch, n);
+  if (rc || batch == 0) return rc;
+  const int parts = norm_parts(batch, n);
+  if (parts > kMaxNormParts) return HC_ERR_SCRATCH;  // the array holds kMaxNormParts partial maxima
+  float* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Every slot the expm kernel reads (0 .. parts-1) is written first by the
+  // norm kernel of this same call, so nothing needs clearing beforehand.
+  rc = launch_norm_partials(A, batch, n, scratch, parts, st);
+  if (rc) return rc;
+  const dim3 grid = expm_grid(batch, n);
+#define L(NN) expm_t18_fwd_kernel<NN><<<grid, kExpmThreads, 0, st>>>(A, E, batch, scratch, parts)
   HC_EXPM_SWITCH(n, L)
 #undef L
   return launch_status();

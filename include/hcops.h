@@ -96,6 +96,25 @@ int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch,
                     int n, float* scratch, int64_t scratch_words,
                     int per_matrix, void* stream);
 
+/* The same result as hc_expm_t18_fwd with per_matrix == 0, for callers that
+ * cannot allocate device memory: a plugin or FFI caller that only receives
+ * pointers from a host framework owning all device memory, or a loop that
+ * must not call cudaMalloc because it can synchronise the device. The
+ * caller passes A and E only; the scratch (the per-CTA partial maxima of
+ * ||A||_1, at most 1024 floats) lives in a fixed 4 KB device array inside the
+ * library, which every GPU that loads the library keeps until exit. Limits:
+ * the same batch bound as the other expm entry points (2^34 matrices, else
+ * HC_ERR_BAD_SIZE); a batch that would need more partial maxima than the
+ * array holds is rejected with HC_ERR_SCRATCH. The first call on a device
+ * looks up the array's device address once (cudaGetSymbolAddress); make that
+ * first call before any stream capture. All calls share the one array and it
+ * keeps the last call's contents; every slot a call reads is written earlier
+ * in the same call, so nothing needs clearing, but calls that overlap on the
+ * GPU (for example on two streams at once) race on it.
+ * No counterpart in the reference. */
+int hc_expm_t18_fwd_noalloc(const float* A, float* E, int64_t batch, int n,
+                            void* stream);
+
 /* E = exp(A) by diagonal Pade [7/7] with per-matrix scaling and squaring
  * (Higham 2005, theta_7 = 3.925724783138660 for unit roundoff 2^-24) and an
  * in-register Gauss-Jordan solve with partial pivoting.
