@@ -210,7 +210,7 @@ WarpTuning& warp_tuning() {
 }  // namespace hc
 
 extern "C" int hc_set_mix_tuning(int stage_bytes, int stages, int warps) {
-  if (stage_bytes < 0 || stages < 0 || stages > kWarpMaxStages || warps < 0 || warps > kWarpMaxWarps)
+  if (stage_bytes < 0 || stages < 0 || stages > kRingMaxStages || warps < 0 || warps >= kWarpMaxWarps)
     return HC_ERR_BAD_SIZE;
   hc::warp_tuning() = hc::WarpTuning{stage_bytes, stages, warps};
   return HC_OK;

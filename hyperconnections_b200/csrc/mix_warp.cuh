@@ -1,28 +1,35 @@
-// mix_warp.cuh — warp-autonomous, TMA-fed stream-mixing kernels (fast path).
+// mix_warp.cuh — warp-specialised, TMA-fed stream-mixing kernels (fast path).
 //
-// Every warp of a persistent CTA owns whole tokens (token gw, gw + stride,
-// ...) and its own ring of shared-memory stages with one mbarrier each. Lane 0
-// issues the bulk copies (cp.async.bulk, no multicast) of the warp's next
-// token-slices; all lanes wait on the stage's barrier, compute, and after a
-// __syncwarp lane 0 refills the stage. Warps never wait for one another: there
-// is no CTA-wide barrier, so the SM always has independent warps to issue
-// from, and the bytes in flight per SM are warps x stages x stage bytes.
+// A persistent CTA per SM owns a contiguous range of tokens and a ring of
+// shared-memory stages, each with a "full" and an "empty" mbarrier. Warp 0 is
+// the producer: one lane issues the bulk copies (cp.async.bulk, no multicast)
+// of the next token (or token-slice) into the next free stage with
+// arrive.expect_tx on its full barrier. Warps 1..C are consumers: consumer c
+// takes tokens c, c + C, ... of the range, waits on the stage's full barrier,
+// computes in fp32 registers, stores 8-byte coalesced words to global memory,
+// and releases the stage by arriving on its empty barrier. No CTA-wide
+// barrier is needed in the steady state, consumers never issue copies, and
+// stage indices and phases advance incrementally (no division per item).
 //
 // A stage holds one token-slice of every input row the kernel needs:
 //   forward  fused: x (n rows), f (1)          add: x (n), Y (n)
 //   backward fused: g_x (n), x (n), g_u (1), f (1)   add: g (n), x (n)
-// laid out [tensor][row][pitch]. When a token fits one slice the rows of one
-// tensor are contiguous in HBM and land with ONE bulk copy per tensor.
+// laid out [tensor][row][pitch]. A token that fits one stage (the usual case)
+// is ONE contiguous bulk copy per tensor; wider tokens are cut into slices,
+// one copy per row slice, and the ring order interleaves the slices of the C
+// tokens in flight so that every consumer always has its next slice coming.
 //
-// Lane l of a warp reads W consecutive 32-bit words of every row at word
+// Lane l of a consumer reads W consecutive 32-bit words of every row at word
 // offset seg*32*W + l*W (conflict-free shared-memory reads, coalesced global
-// stores). Because a token stays on one warp, the backward's per-token sums
-// (grad_Phi / grad_H, grad_alpha, grad_beta, the projection terms) accumulate
-// in registers over all slices and fold with one warp transpose-reduce.
+// stores). A token stays on one consumer warp, so the backward's per-token
+// sums (grad_Phi / grad_H, grad_alpha, grad_beta, the projection terms)
+// accumulate in registers over all slices and fold with one warp
+// transpose-reduce.
 //
-// Every wait is bounded (kWaitLimit polls); a warp that gives up counts it in
-// a device counter (hc_wait_timeouts), drains its own copies with another
-// bounded wait and stops.
+// Every wait is bounded (kWaitLimit polls). A warp that gives up counts it in
+// a device counter (hc_wait_timeouts) and raises the CTA's abort flag; all
+// warps stop, and before the CTA exits one thread waits (bounded again) for
+// every copy the producer issued, so none lands after the CTA is gone.
 #pragma once
 
 #include <algorithm>
@@ -70,12 +77,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kWarpMaxStages = 8;
-constexpr int kWarpMaxWarps = 16;
+constexpr int kRingMaxStages = 32;  // stages of the per-CTA ring
+constexpr int kWarpMaxWarps = 16;   // producer + consumers
 
 // Count of bounded waits that gave up (one counter per translation unit; read
 // and cleared by hc_wait_timeouts()).
 static __device__ unsigned int g_mix_wait_timeouts;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kWaitLimit; ++i)
@@ -148,8 +159,8 @@ __device__ __forceinline__ void stg_words(void* p, const uint32_t* w) {
 
 // ------------------------------------------------------------------ geometry
 struct WarpGeometry {
-  int warps;        // warps per CTA
-  int stages;       // stages per warp
+  int consumers;    // consumer warps per CTA (one producer warp besides)
+  int stages;       // stages of the CTA's ring
   int sl;           // elements per slice
   int ns;           // slices per token
   int pitch;        // shared-memory row pitch (elements)
@@ -158,9 +169,12 @@ struct WarpGeometry {
   int smem_bytes;   // dynamic shared memory per CTA
 };
 
-// Issue the bulk copies of one token-slice into a stage.
+// Warps per CTA at most: 16 (128 registers per thread) for n <= 4, 8 above.
+constexpr int warp_cap(int n) { return n <= 4 ? kWarpMaxWarps : kWarpMaxWarps / 2; }
+
+// Issue the bulk copies of one token-slice into a stage (producer lane).
 template <typename T, int NIN>
-__device__ __forceinline__ void warp_issue(const WarpGeometry& geo, int64_t D, uint8_t* stage, uint64_t* bar,
+__device__ __forceinline__ void ring_issue(const WarpGeometry& geo, int64_t D, uint8_t* stage, uint64_t* bar,
                                            int64_t t, int p, const void* const* base, const int* rows) {
   constexpr int es = sizeof(T);
   const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
@@ -182,6 +196,117 @@ __device__ __forceinline__ void warp_issue(const WarpGeometry& geo, int64_t D, u
     }
     dst += static_cast<size_t>(rows[k]) * geo.pitch * es;
   }
+}
+
+// Shared-memory state of the ring.
+struct RingState {
+  uint64_t full[kRingMaxStages];
+  uint64_t empty[kRingMaxStages];
+  // Item index of the fill most recently started in each stage. A stage is
+  // shared by items of different consumers in successive rounds, and a parity
+  // wait can only tell adjacent phases apart: a consumer that reached item k
+  // while item k - S (another consumer's) was still landing would see the
+  // wrong phase as complete. Consumers therefore wait for tag == k first.
+  volatile long long tag[kRingMaxStages];
+  uint32_t last_parity[kRingMaxStages];  // parity of the last fill issued into each stage
+  int issued[kRingMaxStages];
+  volatile int abort;
+};
+
+__device__ __forceinline__ void ring_init(RingState& st, int stages) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&st.full[s], 1);
+      mbar_init(&st.empty[s], 1);
+      st.tag[s] = -1;
+      st.issued[s] = 0;
+      st.last_parity[s] = 0;
+    }
+    st.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+}
+
+// Producer loop (one lane): fills stages in ring order. Item order within a
+// group of C tokens: slice-major, so consecutive items of one consumer are C
+// apart and each consumer has its next slice in flight.
+template <typename T, int NIN>
+__device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& geo, uint8_t* smem, int64_t D,
+                                             int64_t t_begin, int ntok, const void* const* base, const int* rows) {
+  const int S = geo.stages, C = geo.consumers;
+  int s = 0;
+  uint32_t ph = 0;
+  int64_t k = 0;
+  for (int g0 = 0; g0 < ntok; g0 += C) {
+    const int Wg = min(C, ntok - g0);
+    for (int p = 0; p < geo.ns; ++p) {
+      for (int w = 0; w < Wg; ++w) {
+        if (st.abort) return;
+        if (k >= S) {  // wait until the consumer of item k - S released this stage
+          if (!warp_wait(&st.empty[s], ph ^ 1u)) {
+            atomicAdd(&g_mix_wait_timeouts, 1u);
+            st.abort = 1;
+            return;
+          }
+          fence_proxy_async_smem();
+        }
+        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s], t_begin + g0 + w, p,
+                           base, rows);
+        __threadfence_block();  // the arrive.expect_tx above is visible before the tag
+        st.tag[s] = k;
+        st.issued[s] = 1;
+        st.last_parity[s] = ph;
+        ++k;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  }
+}
+
+// Before the CTA exits: wait (bounded) for the last fill of every stage, so
+// that no copy is still in flight (immediate in a normal run).
+__device__ __forceinline__ void ring_drain(RingState& st, int stages) {
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int s = 0; s < stages; ++s)
+      if (st.issued[s]) warp_wait(&st.full[s], st.last_parity[s]);
+}
+
+// Consumer-side cursor over the ring: item k = g0*ns + p*Wg + c; stage and
+// parity advance by the distance to the consumer's next item.
+struct RingCursor {
+  int s;
+  uint32_t ph;
+  long long k;  // item index
+  __device__ __forceinline__ void advance(int delta, int S) {
+    k += delta;
+    s += delta;
+    if (s >= S) {
+      s -= S;
+      ph ^= 1u;
+    }
+  }
+};
+
+// Consumer wait for its item: first until the producer has started this
+// item's fill (tag), then on the fill's phase. Bounded; warp-uniform result.
+__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur) {
+  bool ok = false;
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (st.tag[cur.s] == cur.k) {
+      ok = true;
+      break;
+    }
+    if (st.abort) break;
+    __nanosleep(32);
+  }
+  __threadfence_block();
+  if (ok) ok = warp_wait(&st.full[cur.s], cur.ph);
+  return __all_sync(kFull, ok);
 }
 
 // Per-token parameters in registers.
@@ -211,353 +336,359 @@ struct TokParams {
 };
 
 // ================================================================= forward
-// Warps per CTA at most: 16 (128 registers per thread) for n <= 4, 8 above.
-constexpr int warp_cap(int n) { return n <= 4 ? kWarpMaxWarps : kWarpMaxWarps / 2; }
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+__device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
+                                          const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len, int lane) {
+  using Wd = Word<T>;
+  constexpr int K = Wd::K;
+  constexpr int NS = FUSED ? 1 : N;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* ot = static_cast<T*>(a.out) + t * N * D + d0;
+  T* ut = FUSED ? static_cast<T*>(a.u) + t * D + d0 : nullptr;
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    Words<W> xw[N], sw[NS];
+#pragma unroll
+    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(q + j * rowb);
+#pragma unroll
+    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(q + (N + i2) * rowb);
+    uint32_t ow[N][W], uw[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float xe[N][K], se[NS][K];
+#pragma unroll
+      for (int j = 0; j < N; ++j) Wd::get(xw[j].w[w], xe[j]);
+#pragma unroll
+      for (int i2 = 0; i2 < NS; ++i2) Wd::get(sw[i2].w[w], se[i2]);
+      float av[K];
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc = fmaf(pr.vv[j], xe[j][e], acc);
+          av[e] = acc;
+        }
+      }
+      if constexpr (FUSED) {
+        float uo[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc = fmaf(pr.al[j], xe[j][e], acc);
+          uo[e] = acc;
+        }
+        uw[w] = Wd::put(uo);
+      }
+#pragma unroll
+      for (int i2 = 0; i2 < N; ++i2) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc = fmaf(pr.phi[i2 * N + j], xe[j][e], acc);
+          if constexpr (PROJ) acc = fmaf(pr.cc[i2], av[e], acc);
+          if constexpr (FUSED) {
+            acc = fmaf(pr.be[i2], se[0][e], acc);
+          } else {
+            acc = acc + se[i2][e];
+          }
+          o[e] = acc;
+        }
+        ow[i2][w] = Wd::put(o);
+      }
+    }
+#pragma unroll
+    for (int i2 = 0; i2 < N; ++i2) stg_words<W>(ot + i2 * D + e0, ow[i2]);
+    if constexpr (FUSED) stg_words<W>(ut + e0, uw);
+  }
+}
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __global__ void __launch_bounds__(warp_cap(N) * 32, 1)
 mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
-  using Wd = Word<T>;
-  constexpr int K = Wd::K;
-  constexpr int NS = FUSED ? 1 : N;  // rows of the second input
-  constexpr int es = sizeof(T);
-  constexpr int SEGW = 32 * W * K;   // elements per warp access
+  constexpr int NS = FUSED ? 1 : N;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bars[kWarpMaxWarps][kWarpMaxStages];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* wsm = smem + static_cast<size_t>(warp) * geo.stages * geo.stage_bytes;
-  uint64_t* full = bars[warp];
-  if (lane == 0) {
-    for (int s = 0; s < geo.stages; ++s) mbar_init(&full[s], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
+  __shared__ RingState st;
+  ring_init(st, geo.stages);
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * geo.warps + warp;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * geo.warps;
-  const int64_t ntok = gw < T_ ? (T_ - gw + stride - 1) / stride : 0;
-  const int64_t nitems = ntok * geo.ns;
-  const void* base[2] = {a.x, a.src};
-  const int rows[2] = {N, NS};
-  const size_t rowb = static_cast<size_t>(geo.pitch) * es;
+  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
+  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = geo.stages, C = geo.consumers, ns = geo.ns;
 
-  if (lane == 0)
-    for (int64_t i = 0; i < nitems && i < geo.stages; ++i)
-      warp_issue<T, 2>(geo, D, wsm + i * geo.stage_bytes, &full[i], gw + (i / geo.ns) * stride,
-                       static_cast<int>(i % geo.ns), base, rows);
-
-  TokParams<P, N, FUSED, PROJ> pr;
-  int64_t i = 0;
-  bool aborted = false;
-  for (; i < nitems; ++i) {
-    const int s = static_cast<int>(i % geo.stages);
-    const int64_t t = gw + (i / geo.ns) * stride;
-    const int p = static_cast<int>(i % geo.ns);
-    if (p == 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
-    if (!__all_sync(kFull, warp_wait(&full[s], static_cast<uint32_t>((i / geo.stages) & 1)))) {
-      aborted = true;
-      break;
+  if (warp == 0) {
+    if (lane == 0) {
+      const void* base[2] = {a.x, a.src};
+      const int rows[2] = {N, NS};
+      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, base, rows);
     }
-    const uint8_t* sb = wsm + static_cast<size_t>(s) * geo.stage_bytes;
-    const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
-    const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-    T* ot = static_cast<T*>(a.out) + t * N * D + d0;
-    T* ut = FUSED ? static_cast<T*>(a.u) + t * D + d0 : nullptr;
-    for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-      const uint8_t* q = sb + static_cast<size_t>(e0) * es;
-      Words<W> xw[N], sw[NS];
-#pragma unroll
-      for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(q + j * rowb);
-#pragma unroll
-      for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(q + (N + i2) * rowb);
-      uint32_t ow[N][W], uw[W];
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        float xe[N][K], se[NS][K];
-#pragma unroll
-        for (int j = 0; j < N; ++j) Wd::get(xw[j].w[w], xe[j]);
-#pragma unroll
-        for (int i2 = 0; i2 < NS; ++i2) Wd::get(sw[i2].w[w], se[i2]);
-        float av[K];
-        if constexpr (PROJ) {
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc = fmaf(pr.vv[j], xe[j][e], acc);
-            av[e] = acc;
+  } else if (warp - 1 < C) {
+    const int c = warp - 1;
+    TokParams<P, N, FUSED, PROJ> pr;
+    RingCursor cur{c, 0u, c};
+    for (int g0 = 0; g0 < ntok; g0 += C) {
+      const int Wg = min(C, ntok - g0);
+      if (c >= Wg) break;
+      const int64_t t = t_begin + g0 + c;
+      pr.load(a.phi, a.v, a.alpha, a.beta, t);
+      for (int p = 0; p < ns; ++p) {
+        if (__any_sync(kFull, st.abort)) break;
+        if (!ring_wait_item(st, cur)) {
+          if (lane == 0 && !st.abort) {
+            atomicAdd(&g_mix_wait_timeouts, 1u);
+            st.abort = 1;
           }
+          break;
         }
-        if constexpr (FUSED) {
-          float uo[K];
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc = fmaf(pr.al[j], xe[j][e], acc);
-            uo[e] = acc;
-          }
-          uw[w] = Wd::put(uo);
-        }
-#pragma unroll
-        for (int i2 = 0; i2 < N; ++i2) {
-          float o[K];
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc = fmaf(pr.phi[i2 * N + j], xe[j][e], acc);
-            if constexpr (PROJ) acc = fmaf(pr.cc[i2], av[e], acc);
-            if constexpr (FUSED) {
-              acc = fmaf(pr.be[i2], se[0][e], acc);
-            } else {
-              acc = acc + se[i2][e];
-            }
-            o[e] = acc;
-          }
-          ow[i2][w] = Wd::put(o);
-        }
+        const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
+        const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
+        fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch, t,
+                                           d0, len, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st.empty[cur.s]);
+        cur.advance(p + 1 < ns ? Wg : C, S);
       }
-#pragma unroll
-      for (int i2 = 0; i2 < N; ++i2) stg_words<W>(ot + i2 * D + e0, ow[i2]);
-      if constexpr (FUSED) stg_words<W>(ut + e0, uw);
-    }
-    __syncwarp();
-    if (lane == 0 && i + geo.stages < nitems) {
-      fence_proxy_async_smem();
-      const int64_t in = i + geo.stages;
-      warp_issue<T, 2>(geo, D, wsm + static_cast<size_t>(s) * geo.stage_bytes, &full[s],
-                       gw + (in / geo.ns) * stride, static_cast<int>(in % geo.ns), base, rows);
+      if (__any_sync(kFull, st.abort)) break;
     }
   }
-  if (aborted && lane == 0) {
-    atomicAdd(&g_mix_wait_timeouts, 1u);
-    for (int64_t j = i; j < nitems && j < i + geo.stages; ++j)  // drain this warp's copies
-      warp_wait(&full[j % geo.stages], static_cast<uint32_t>((j / geo.stages) & 1));
-  }
+  ring_drain(st, S);
 }
 
 // ================================================================= backward
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
-__global__ void __launch_bounds__(warp_cap(N) * 32, 1)
-mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
+__device__ __forceinline__ void bwd_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
+                                          float* acc, const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len,
+                                          int lane) {
   using Wd = Word<T>;
-  using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int K = Wd::K;
-  constexpr int R = L::kR;
   constexpr int es = sizeof(T);
   constexpr int SEGW = 32 * W * K;
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
+  T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    Words<W> gw_[N], xw[N], uw, fw;
+#pragma unroll
+    for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(q + r * rowb);
+#pragma unroll
+    for (int r = 0; r < N; ++r) xw[r] = lds_words<W>(q + (N + r) * rowb);
+    if constexpr (FUSED) {
+      uw = lds_words<W>(q + (2 * N) * rowb);
+      fw = lds_words<W>(q + (2 * N + 1) * rowb);
+    }
+    uint32_t gxo[N][W], gfo[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float ge[N][K], xe[N][K], gue[K], fe[K];
+#pragma unroll
+      for (int r = 0; r < N; ++r) Wd::get(gw_[r].w[w], ge[r]);
+#pragma unroll
+      for (int r = 0; r < N; ++r) Wd::get(xw[r].w[w], xe[r]);
+      if constexpr (FUSED) {
+        Wd::get(uw.w[w], gue);
+        Wd::get(fw.w[w], fe);
+      }
+      float av[K], bt[K];
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float sa = 0.f, sb2 = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) sa = fmaf(pr.vv[j], xe[j][e], sa);
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) sb2 = fmaf(ge[i2][e], pr.cc[i2], sb2);
+          av[e] = sa;
+          bt[e] = sb2;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float sacc = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) sacc = fmaf(pr.phi[i2 * N + j], ge[i2][e], sacc);
+          if constexpr (PROJ) sacc = fmaf(pr.vv[j], bt[e], sacc);
+          if constexpr (FUSED) sacc = fmaf(pr.al[j], gue[e], sacc);
+          o[e] = sacc;
+        }
+        gxo[j][w] = Wd::put(o);
+      }
+      if constexpr (FUSED) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float sacc = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) sacc = fmaf(pr.be[i2], ge[i2][e], sacc);
+          o[e] = sacc;
+        }
+        gfo[w] = Wd::put(o);
+      }
+#pragma unroll
+      for (int e = 0; e < K; ++e) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          float xv = xe[j][e];
+          if constexpr (PROJ) xv = xv - pr.vv[j] * av[e];
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) acc[i2 * N + j] = fmaf(ge[i2][e], xv, acc[i2 * N + j]);
+        }
+        if constexpr (FUSED) {
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc[N * N + j] = fmaf(gue[e], xe[j][e], acc[N * N + j]);
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) acc[N * N + N + i2] = fmaf(ge[i2][e], fe[e], acc[N * N + N + i2]);
+        }
+        if constexpr (PROJ) {
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) acc[N * N + i2] = fmaf(ge[i2][e], av[e], acc[N * N + i2]);
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc[N * N + N + j] = fmaf(bt[e], xe[j][e], acc[N * N + N + j]);
+        }
+      }
+    }
+    if (gxt) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) stg_words<W>(gxt + j * D + e0, gxo[j]);
+    }
+    if constexpr (FUSED) {
+      if (gft) stg_words<W>(gft + e0, gfo);
+    }
+  }
+}
+
+// Fold the 32 lanes' partial sums of one token and write its parameter
+// gradients (and grad_v for the projection).
+template <typename P, int N, bool FUSED, bool PROJ>
+__device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
+                                           const float* acc, int64_t t, int lane) {
+  using L = BwdLayout<N, FUSED, PROJ>;
+  constexpr int R = L::kR;
+  float v[L::kPad];
+#pragma unroll
+  for (int k = 0; k < L::kPad; ++k) v[k] = acc[k];
+  warp_transpose_reduce<R>(v, lane);  // lane l now holds sums [R*l, R*l + R)
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int k = lane * R + r;
+    if (k < N * N) {
+      if (a.grad_phi) a.grad_phi[t * (N * N) + k] = v[r];
+    } else if (k < L::kAcc) {
+      if constexpr (FUSED) {
+        if (k < N * N + N) {
+          if (a.grad_alpha) a.grad_alpha[t * N + (k - N * N)] = v[r];
+        } else {
+          if (a.grad_beta) a.grad_beta[t * N + (k - N * N - N)] = v[r];
+        }
+      }
+    }
+  }
+  if constexpr (PROJ) {
+    // grad_v_j = rho_j - sum_i Phi_ij rho_i + beta-part_j
+    // (reference ops/stream_mix_small_nb.py:379-384)
+    float rho[N], bp[N];
+#pragma unroll
+    for (int q2 = 0; q2 < N; ++q2) {
+      rho[q2] = __shfl_sync(kFull, v[(N * N + q2) % R], (N * N + q2) / R);
+      bp[q2] = __shfl_sync(kFull, v[(N * N + N + q2) % R], (N * N + N + q2) / R);
+    }
+    if (a.grad_v != nullptr && lane < N) {
+      float out = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        if (j == lane) {
+          float ptr = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) ptr = fmaf(pr.phi[i2 * N + j], rho[i2], ptr);
+          out = (rho[j] - ptr) + bp[j];
+        }
+      }
+      a.grad_v[t * N + lane] = out;
+    }
+  }
+}
+
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+__global__ void __launch_bounds__(warp_cap(N) * 32, 1)
+mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
+  using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bars[kWarpMaxWarps][kWarpMaxStages];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* wsm = smem + static_cast<size_t>(warp) * geo.stages * geo.stage_bytes;
-  uint64_t* full = bars[warp];
-  if (lane == 0) {
-    for (int s = 0; s < geo.stages; ++s) mbar_init(&full[s], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
+  __shared__ RingState st;
+  ring_init(st, geo.stages);
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * geo.warps + warp;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * geo.warps;
-  const int64_t ntok = gw < T_ ? (T_ - gw + stride - 1) / stride : 0;
-  const int64_t nitems = ntok * geo.ns;
-  const void* base[NIN];
-  int rows[NIN];
-  base[0] = a.g;
-  base[1] = a.x;
-  rows[0] = N;
-  rows[1] = N;
-  if constexpr (FUSED) {
-    base[2] = a.gu;
-    base[3] = a.f;
-    rows[2] = 1;
-    rows[3] = 1;
-  }
-  const size_t rowb = static_cast<size_t>(geo.pitch) * es;
+  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
+  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = geo.stages, C = geo.consumers, ns = geo.ns;
 
-  if (lane == 0)
-    for (int64_t i = 0; i < nitems && i < geo.stages; ++i)
-      warp_issue<T, NIN>(geo, D, wsm + i * geo.stage_bytes, &full[i], gw + (i / geo.ns) * stride,
-                         static_cast<int>(i % geo.ns), base, rows);
-
-  TokParams<P, N, FUSED, PROJ> pr;
-  float acc[L::kPad];
-  int64_t i = 0;
-  bool aborted = false;
-  for (; i < nitems; ++i) {
-    const int s = static_cast<int>(i % geo.stages);
-    const int64_t t = gw + (i / geo.ns) * stride;
-    const int p = static_cast<int>(i % geo.ns);
-    if (p == 0) {
+  if (warp == 0) {
+    if (lane == 0) {
+      const void* base[NIN];
+      int rows[NIN];
+      base[0] = a.g;
+      base[1] = a.x;
+      rows[0] = N;
+      rows[1] = N;
+      if constexpr (FUSED) {
+        base[2] = a.gu;
+        base[3] = a.f;
+        rows[2] = 1;
+        rows[3] = 1;
+      }
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, base, rows);
+    }
+  } else if (warp - 1 < C) {
+    const int c = warp - 1;
+    TokParams<P, N, FUSED, PROJ> pr;
+    float acc[L::kPad];
+    RingCursor cur{c, 0u, c};
+    for (int g0 = 0; g0 < ntok; g0 += C) {
+      const int Wg = min(C, ntok - g0);
+      if (c >= Wg) break;
+      const int64_t t = t_begin + g0 + c;
       pr.load(a.phi, a.v, a.alpha, a.beta, t);
 #pragma unroll
       for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
-    }
-    if (!__all_sync(kFull, warp_wait(&full[s], static_cast<uint32_t>((i / geo.stages) & 1)))) {
-      aborted = true;
-      break;
-    }
-    const uint8_t* sb = wsm + static_cast<size_t>(s) * geo.stage_bytes;
-    const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
-    const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-    T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
-    T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
-    for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-      const uint8_t* q = sb + static_cast<size_t>(e0) * es;
-      Words<W> gw_[N], xw[N], uw, fw;
-#pragma unroll
-      for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(q + r * rowb);
-#pragma unroll
-      for (int r = 0; r < N; ++r) xw[r] = lds_words<W>(q + (N + r) * rowb);
-      if constexpr (FUSED) {
-        uw = lds_words<W>(q + (2 * N) * rowb);
-        fw = lds_words<W>(q + (2 * N + 1) * rowb);
+      bool done = true;
+      for (int p = 0; p < ns; ++p) {
+        if (__any_sync(kFull, st.abort)) {
+          done = false;
+          break;
+        }
+        if (!ring_wait_item(st, cur)) {
+          if (lane == 0 && !st.abort) {
+            atomicAdd(&g_mix_wait_timeouts, 1u);
+            st.abort = 1;
+          }
+          done = false;
+          break;
+        }
+        const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
+        const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
+        bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
+                                           geo.pitch, t, d0, len, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st.empty[cur.s]);
+        cur.advance(p + 1 < ns ? Wg : C, S);
       }
-      uint32_t gxo[N][W], gfo[W];
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        float ge[N][K], xe[N][K], gue[K], fe[K];
-#pragma unroll
-        for (int r = 0; r < N; ++r) Wd::get(gw_[r].w[w], ge[r]);
-#pragma unroll
-        for (int r = 0; r < N; ++r) Wd::get(xw[r].w[w], xe[r]);
-        if constexpr (FUSED) {
-          Wd::get(uw.w[w], gue);
-          Wd::get(fw.w[w], fe);
-        }
-        float av[K], bt[K];
-        if constexpr (PROJ) {
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float sa = 0.f, sb2 = 0.f;
-#pragma unroll
-            for (int j = 0; j < N; ++j) sa = fmaf(pr.vv[j], xe[j][e], sa);
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) sb2 = fmaf(ge[i2][e], pr.cc[i2], sb2);
-            av[e] = sa;
-            bt[e] = sb2;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          float o[K];
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float sacc = 0.f;
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) sacc = fmaf(pr.phi[i2 * N + j], ge[i2][e], sacc);
-            if constexpr (PROJ) sacc = fmaf(pr.vv[j], bt[e], sacc);
-            if constexpr (FUSED) sacc = fmaf(pr.al[j], gue[e], sacc);
-            o[e] = sacc;
-          }
-          gxo[j][w] = Wd::put(o);
-        }
-        if constexpr (FUSED) {
-          float o[K];
-#pragma unroll
-          for (int e = 0; e < K; ++e) {
-            float sacc = 0.f;
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) sacc = fmaf(pr.be[i2], ge[i2][e], sacc);
-            o[e] = sacc;
-          }
-          gfo[w] = Wd::put(o);
-        }
-#pragma unroll
-        for (int e = 0; e < K; ++e) {
-#pragma unroll
-          for (int j = 0; j < N; ++j) {
-            float xv = xe[j][e];
-            if constexpr (PROJ) xv = xv - pr.vv[j] * av[e];
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) acc[i2 * N + j] = fmaf(ge[i2][e], xv, acc[i2 * N + j]);
-          }
-          if constexpr (FUSED) {
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc[N * N + j] = fmaf(gue[e], xe[j][e], acc[N * N + j]);
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) acc[N * N + N + i2] = fmaf(ge[i2][e], fe[e], acc[N * N + N + i2]);
-          }
-          if constexpr (PROJ) {
-#pragma unroll
-            for (int i2 = 0; i2 < N; ++i2) acc[N * N + i2] = fmaf(ge[i2][e], av[e], acc[N * N + i2]);
-#pragma unroll
-            for (int j = 0; j < N; ++j) acc[N * N + N + j] = fmaf(bt[e], xe[j][e], acc[N * N + N + j]);
-          }
-        }
-      }
-      if (gxt) {
-#pragma unroll
-        for (int j = 0; j < N; ++j) stg_words<W>(gxt + j * D + e0, gxo[j]);
-      }
-      if constexpr (FUSED) {
-        if (gft) stg_words<W>(gft + e0, gfo);
-      }
-    }
-    __syncwarp();
-    if (lane == 0 && i + geo.stages < nitems) {
-      fence_proxy_async_smem();
-      const int64_t in = i + geo.stages;
-      warp_issue<T, NIN>(geo, D, wsm + static_cast<size_t>(s) * geo.stage_bytes, &full[s],
-                         gw + (in / geo.ns) * stride, static_cast<int>(in % geo.ns), base, rows);
-    }
-    if (p == geo.ns - 1) {
-      // this warp's token is complete: fold the 32 lanes' partial sums
-      float v[L::kPad];
-#pragma unroll
-      for (int k = 0; k < L::kPad; ++k) v[k] = acc[k];
-      warp_transpose_reduce<R>(v, lane);  // lane l now holds sums [R*l, R*l + R)
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int k = lane * R + r;
-        if (k < N * N) {
-          if (a.grad_phi) a.grad_phi[t * (N * N) + k] = v[r];
-        } else if (k < L::kAcc) {
-          if constexpr (FUSED) {
-            if (k < N * N + N) {
-              if (a.grad_alpha) a.grad_alpha[t * N + (k - N * N)] = v[r];
-            } else {
-              if (a.grad_beta) a.grad_beta[t * N + (k - N * N - N)] = v[r];
-            }
-          }
-        }
-      }
-      if constexpr (PROJ) {
-        // grad_v_j = rho_j - sum_i Phi_ij rho_i + beta-part_j
-        // (reference ops/stream_mix_small_nb.py:379-384)
-        float rho[N], bp[N];
-#pragma unroll
-        for (int q2 = 0; q2 < N; ++q2) {
-          rho[q2] = __shfl_sync(kFull, v[(N * N + q2) % R], (N * N + q2) / R);
-          bp[q2] = __shfl_sync(kFull, v[(N * N + N + q2) % R], (N * N + N + q2) / R);
-        }
-        if (a.grad_v != nullptr && lane < N) {
-          float out = 0.f;
-#pragma unroll
-          for (int j = 0; j < N; ++j) {
-            if (j == lane) {
-              float ptr = 0.f;
-#pragma unroll
-              for (int i2 = 0; i2 < N; ++i2) ptr = fmaf(pr.phi[i2 * N + j], rho[i2], ptr);
-              out = (rho[j] - ptr) + bp[j];
-            }
-          }
-          a.grad_v[t * N + lane] = out;
-        }
-      }
+      if (!done) break;
+      bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
     }
   }
-  if (aborted && lane == 0) {
-    atomicAdd(&g_mix_wait_timeouts, 1u);
-    for (int64_t j = i; j < nitems && j < i + geo.stages; ++j)
-      warp_wait(&full[j % geo.stages], static_cast<uint32_t>((j / geo.stages) & 1));
-  }
+  ring_drain(st, S);
 }
 
 // ================================================================= host side
@@ -568,13 +699,13 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 
 // Tuning knobs (0 = automatic), set through hc_set_mix_tuning().
 struct WarpTuning {
-  int stage_bytes;  // target bytes of one stage
-  int stages;       // stages per warp
-  int warps;        // warps per CTA
+  int stage_bytes;  // largest stage before a token is cut into slices
+  int stages;       // stages of the ring
+  int warps;        // consumer warps per CTA
 };
 WarpTuning& warp_tuning();
 
-// Geometry of the warp pipeline; false when the shape does not fit it.
+// Geometry of the ring; false when the shape does not fit it.
 // Requires D % (16 / esize) == 0 and 16-byte aligned stream bases.
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
                           int num_sms) {
@@ -582,43 +713,26 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_
   const WarpTuning tune = warp_tuning();
   const int rows = warp_rows(bwd, fused, n);
   const int budget = 200 * 1024;
-  const int wcap = warp_cap(n);
-  int stages = tune.stages > 0 ? std::min(tune.stages, kWarpMaxStages) : 2;
-  if (stages < 2) stages = 2;
-  // slice: the whole token when its rows fit the stage target, else a
-  // multiple of 64 elements
-  const int64_t target =
-      tune.stage_bytes > 0 ? tune.stage_bytes : std::max<int64_t>(2048, budget / (stages * wcap));
+  const int64_t max_stage = tune.stage_bytes > 0 ? tune.stage_bytes : 24 * 1024;
   int64_t sl = D;
-  if (rows * D * esize > target) {
-    sl = std::max<int64_t>(64, (target / (rows * esize)) / 64 * 64);
+  if (static_cast<int64_t>(rows) * D * esize > max_stage) {
+    const int64_t slice_target = tune.stage_bytes > 0 ? tune.stage_bytes : 16 * 1024;
+    sl = std::max<int64_t>(64, (slice_target / (rows * esize)) / 64 * 64);
     if (sl >= D) sl = D;
   }
   geo.sl = static_cast<int>(sl);
   geo.ns = static_cast<int>((D + sl - 1) / sl);
   geo.pitch = geo.sl;
   geo.stage_bytes = static_cast<int>(rows * sl * esize);
-  int wmax = budget / (stages * geo.stage_bytes);
-  if (wmax > wcap) wmax = wcap;
-  if (tune.warps > 0) wmax = std::min(wmax, tune.warps);
-  if (wmax < 1) return false;
-  // warps per CTA: among the last few counts that fit, the one whose last
-  // round of tokens is fullest (tokens are dealt round-robin to warps)
-  int best = wmax;
-  double best_eff = 0.0;
-  for (int w = wmax; w >= std::max(1, wmax - 4); --w) {
-    const int64_t grid = std::min<int64_t>(num_sms, (T + w - 1) / w);
-    const double per = static_cast<double>(T) / (grid * w);
-    const double eff = per / std::ceil(per);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
-      best = w;
-    }
-  }
-  geo.warps = best;
+  int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
+  if (tune.stages > 0) stages = std::min(stages, tune.stages);
+  int consumers = std::min(warp_cap(n) - 1, stages - 2);
+  if (tune.warps > 0) consumers = std::min(consumers, tune.warps);
+  if (consumers < 1 || stages < 3) return false;
   geo.stages = stages;
-  geo.smem_bytes = best * stages * geo.stage_bytes;
-  geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, (T + best - 1) / best)));
+  geo.consumers = consumers;
+  geo.smem_bytes = stages * geo.stage_bytes;
+  geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
   return true;
 }
 
@@ -633,7 +747,7 @@ constexpr int kWarpW = 2;  // 32-bit words per lane access (8-byte accesses)
 
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cudaStream_t s) {
-  const dim3 block(geo.warps * 32, 1, 1);
+  const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
@@ -651,7 +765,7 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cud
 
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_bwd_warp(int n, const WarpGeometry& geo, const MixBwdArgs& a, cudaStream_t s) {
-  const dim3 block(geo.warps * 32, 1, 1);
+  const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
@@ -667,7 +781,7 @@ int launch_mix_bwd_warp(int n, const WarpGeometry& geo, const MixBwdArgs& a, cud
   return launch_status();
 }
 
-// Per-dtype entry points of the warp-pipelined kernels (mix_*.cu).
+// Per-dtype entry points of the ring kernels (mix_*.cu).
 #define HC_DECLARE_WARP(SFX)                                                                                 \
   int mix_fwd_warp_##SFX(bool fused, bool proj, bool param_is_f32, int n, const WarpGeometry& g,             \
                          const MixFwdArgs& a, cudaStream_t s);                                               \

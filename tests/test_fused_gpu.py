@@ -165,3 +165,25 @@ def test_fused_errors():
               torch.randn(4, 9, device=DEVICE))
     with pytest.raises(AssertionError):
         fused(x, f[:, :32], H, alpha, beta)
+
+
+@pytest.mark.parametrize("n,D,T,dtype", [
+    (2, 2048, 4000, torch.bfloat16),   # whole-token stages, several ring rounds per CTA
+    (4, 768, 6000, torch.bfloat16),
+    (3, 1024, 5000, torch.float16),
+    (8, 4096, 1200, torch.bfloat16),   # tokens cut into slices
+    (6, 2048, 2500, torch.float32),
+])
+def test_fused_many_tokens_per_cta(n, D, T, dtype):
+    """Every CTA of the pipelined kernels walks many tokens (several rounds of
+    its shared-memory ring): outputs and the wait-timeout counter."""
+    from hyperconnections_b200 import _lib
+
+    inputs = workload(T, n, D, dtype, seed=T + n)
+    for _ in range(3):  # repeated launches: a stale phase would show up here
+        u, x_out, grads = run(*inputs)
+    if dtype == torch.float32:
+        check(u, x_out, grads, inputs, 1e-5, rel=True)
+    else:
+        check(u, x_out, grads, inputs, 2e-2, rel=False)
+    assert _lib.wait_timeouts() == 0

@@ -264,3 +264,28 @@ def test_golden_reference_triton_fp16(case):
     out = stream_mix_add(g("Phi"), g("x"), g("Y"))
     # both sides accumulate in fp32 and round once to fp16
     assert_half(out, MIX16[f"{case}_out"].astype(np.float64), 1e-2, "out")
+
+
+@pytest.mark.parametrize("B,N,D,proj", [(3000, 4, 1024, True), (5000, 2, 2048, False), (800, 8, 4096, True)])
+def test_many_tokens_per_cta(B, N, D, proj):
+    """The pipelined kernels with many tokens per CTA, bf16 streams, repeated
+    launches: forward and backward against the oracle."""
+    from hyperconnections_b200 import _lib
+
+    Phi, x, Y = make_inputs(B, N, D, dtype=torch.bfloat16)
+    v = make_v(B, N) if proj else None
+    torch.manual_seed(3)
+    Gup = torch.randn(B, N, D).to(torch.bfloat16).to(DEVICE)
+    for _ in range(3):
+        P_t, x_t = Phi.detach().requires_grad_(True), x.detach().requires_grad_(True)
+        v_t = v.detach().requires_grad_(True) if proj else None
+        out = stream_mix_add(P_t, x_t, Y, v=v_t)
+        out.backward(Gup)
+    ref = omix.stream_mix_fwd(np64(Phi), np64(x), np64(Y), np64(v))
+    rP, rx, _, rv = omix.stream_mix_bwd(np64(Gup), np64(Phi), np64(x), np64(v))
+    assert_half(out, ref, 2e-2, "out")
+    assert_half(x_t.grad, rx, 2e-2, "grad_x")
+    assert np.abs(np64(P_t.grad) - rP).max() <= 1e-2 * np.abs(rP).max()
+    if proj:
+        assert np.abs(np64(v_t.grad) - rv).max() <= 1e-2 * np.abs(rv).max()
+    assert _lib.wait_timeouts() == 0
