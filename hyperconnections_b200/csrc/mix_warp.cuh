@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <type_traits>
 
 #include "mix_kernels.cuh"
 
@@ -169,8 +170,12 @@ struct WarpGeometry {
   int smem_bytes;   // dynamic shared memory per CTA
 };
 
-// Warps per CTA at most: 16 (128 registers per thread) for n <= 4, 8 above.
-constexpr int warp_cap(int n) { return n <= 4 ? kWarpMaxWarps : kWarpMaxWarps / 2; }
+// Warps per CTA at most (producer included). The forward keeps 16 warps (128
+// registers per thread) for n <= 4; the packed-pair backward for n <= 4 needs
+// up to 170 registers, so 12 warps; larger n use 8 warps (255 registers).
+constexpr int fwd_warp_cap(int n) { return n <= 4 ? 16 : 8; }
+constexpr int bwd_warp_cap(int n) { return n <= 4 ? 12 : 8; }
+constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap(n) : fwd_warp_cap(n); }
 
 // Issue the bulk copies of one token-slice into a stage (producer lane).
 template <typename T, int NIN>
@@ -335,6 +340,229 @@ struct TokParams {
   }
 };
 
+// ------------------------------------------------------------ packed pairs
+// For n <= 4 the kernels run on pairs of elements with fma.rn.f32x2
+// (__ffma2_rn): two independent fp32 FMAs per instruction on a register pair,
+// with the per-token parameters duplicated into pairs. A 32-bit word of
+// bf16/fp16 holds exactly one pair; fp32 streams pair two consecutive words.
+// Every element still sees one fp32 FMA per term, in the same order.
+constexpr bool use_pairs(int n) { return n <= 4; }
+
+__device__ __forceinline__ float2 dup2(float v) { return make_float2(v, v); }
+
+template <typename T> struct PairIO;
+template <> struct PairIO<__nv_bfloat16> {
+  static constexpr int WORDS = 1;
+  __device__ static __forceinline__ float2 get(const uint32_t* w) {
+    return make_float2(__uint_as_float(w[0] << 16), __uint_as_float(w[0] & 0xffff0000u));
+  }
+  __device__ static __forceinline__ void put(float2 v, uint32_t* w) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    w[0] = *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct PairIO<__half> {
+  static constexpr int WORDS = 1;
+  __device__ static __forceinline__ float2 get(const uint32_t* w) {
+    __half2 h = *reinterpret_cast<const __half2*>(w);
+    return __half22float2(h);
+  }
+  __device__ static __forceinline__ void put(float2 v, uint32_t* w) {
+    __half2 h = __floats2half2_rn(v.x, v.y);
+    w[0] = *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct PairIO<float> {
+  static constexpr int WORDS = 2;
+  __device__ static __forceinline__ float2 get(const uint32_t* w) {
+    return make_float2(__uint_as_float(w[0]), __uint_as_float(w[1]));
+  }
+  __device__ static __forceinline__ void put(float2 v, uint32_t* w) {
+    w[0] = __float_as_uint(v.x);
+    w[1] = __float_as_uint(v.y);
+  }
+};
+
+template <typename P, int N, bool FUSED, bool PROJ>
+struct TokParams2 {
+  float2 phi[N * N];
+  float2 vv[PROJ ? N : 1], nvv[PROJ ? N : 1], cc[PROJ ? N : 1];
+  float2 al[FUSED ? N : 1], be[FUSED ? N : 1];
+  __device__ __forceinline__ void load(const void* phi_p, const void* v_p, const float* alpha, const float* beta,
+                                       int64_t t) {
+    TokParams<P, N, FUSED, PROJ> s;
+    s.load(phi_p, v_p, alpha, beta, t);
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) phi[k] = dup2(s.phi[k]);
+    if constexpr (PROJ) {
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        vv[k] = dup2(s.vv[k]);
+        nvv[k] = dup2(-s.vv[k]);
+        cc[k] = dup2(s.cc[k]);
+      }
+    }
+    if constexpr (FUSED) {
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        al[k] = dup2(s.al[k]);
+        be[k] = dup2(s.be[k]);
+      }
+    }
+  }
+};
+
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+__device__ __forceinline__ void fwd_slice2(const MixFwdArgs& a, const TokParams2<P, N, FUSED, PROJ>& pr,
+                                           const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len, int lane) {
+  using IO = PairIO<T>;
+  constexpr int K = Word<T>::K;
+  constexpr int WP = IO::WORDS;
+  constexpr int NS = FUSED ? 1 : N;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  static_assert(W % WP == 0, "lane access must hold whole pairs");
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* ot = static_cast<T*>(a.out) + t * N * D + d0;
+  T* ut = FUSED ? static_cast<T*>(a.u) + t * D + d0 : nullptr;
+  const float2 zero = make_float2(0.f, 0.f);
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    Words<W> xw[N], sw[NS];
+#pragma unroll
+    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(q + j * rowb);
+#pragma unroll
+    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(q + (N + i2) * rowb);
+    uint32_t ow[N][W], uw[W];
+#pragma unroll
+    for (int w = 0; w < W; w += WP) {
+      float2 x[N], sv[NS];
+#pragma unroll
+      for (int j = 0; j < N; ++j) x[j] = IO::get(&xw[j].w[w]);
+#pragma unroll
+      for (int i2 = 0; i2 < NS; ++i2) sv[i2] = IO::get(&sw[i2].w[w]);
+      float2 av = zero;
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) av = __ffma2_rn(pr.vv[j], x[j], av);
+      }
+      if constexpr (FUSED) {
+        float2 u = zero;
+#pragma unroll
+        for (int j = 0; j < N; ++j) u = __ffma2_rn(pr.al[j], x[j], u);
+        IO::put(u, &uw[w]);
+      }
+#pragma unroll
+      for (int i2 = 0; i2 < N; ++i2) {
+        float2 o = zero;
+#pragma unroll
+        for (int j = 0; j < N; ++j) o = __ffma2_rn(pr.phi[i2 * N + j], x[j], o);
+        if constexpr (PROJ) o = __ffma2_rn(pr.cc[i2], av, o);
+        if constexpr (FUSED) {
+          o = __ffma2_rn(pr.be[i2], sv[0], o);
+        } else {
+          o = __fadd2_rn(o, sv[i2]);
+        }
+        IO::put(o, &ow[i2][w]);
+      }
+    }
+#pragma unroll
+    for (int i2 = 0; i2 < N; ++i2) stg_words<W>(ot + i2 * D + e0, ow[i2]);
+    if constexpr (FUSED) stg_words<W>(ut + e0, uw);
+  }
+}
+
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+__device__ __forceinline__ void bwd_slice2(const MixBwdArgs& a, const TokParams2<P, N, FUSED, PROJ>& pr,
+                                           float2* acc, const uint8_t* sb, int pitch, int64_t t, int64_t d0,
+                                           int len, int lane) {
+  using IO = PairIO<T>;
+  constexpr int K = Word<T>::K;
+  constexpr int WP = IO::WORDS;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  static_assert(W % WP == 0, "lane access must hold whole pairs");
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
+  T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
+  const float2 zero = make_float2(0.f, 0.f);
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    Words<W> gwr[N], xwr[N], uwr, fwr;
+#pragma unroll
+    for (int r = 0; r < N; ++r) gwr[r] = lds_words<W>(q + r * rowb);
+#pragma unroll
+    for (int r = 0; r < N; ++r) xwr[r] = lds_words<W>(q + (N + r) * rowb);
+    if constexpr (FUSED) {
+      uwr = lds_words<W>(q + (2 * N) * rowb);
+      fwr = lds_words<W>(q + (2 * N + 1) * rowb);
+    }
+    uint32_t gxo[N][W], gfo[W];
+#pragma unroll
+    for (int w = 0; w < W; w += WP) {
+      float2 g[N], x[N], gu = zero, f = zero;
+#pragma unroll
+      for (int r = 0; r < N; ++r) g[r] = IO::get(&gwr[r].w[w]);
+#pragma unroll
+      for (int r = 0; r < N; ++r) x[r] = IO::get(&xwr[r].w[w]);
+      if constexpr (FUSED) {
+        gu = IO::get(&uwr.w[w]);
+        f = IO::get(&fwr.w[w]);
+      }
+      float2 av = zero, bt = zero;
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) av = __ffma2_rn(pr.vv[j], x[j], av);
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) bt = __ffma2_rn(g[i2], pr.cc[i2], bt);
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float2 o = zero;
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) o = __ffma2_rn(pr.phi[i2 * N + j], g[i2], o);
+        if constexpr (PROJ) o = __ffma2_rn(pr.vv[j], bt, o);
+        if constexpr (FUSED) o = __ffma2_rn(pr.al[j], gu, o);
+        IO::put(o, &gxo[j][w]);
+      }
+      if constexpr (FUSED) {
+        float2 o = zero;
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) o = __ffma2_rn(pr.be[i2], g[i2], o);
+        IO::put(o, &gfo[w]);
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float2 xv = x[j];
+        if constexpr (PROJ) xv = __ffma2_rn(pr.nvv[j], av, xv);  // x_eff = x - v (v^T x)
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) acc[i2 * N + j] = __ffma2_rn(g[i2], xv, acc[i2 * N + j]);
+      }
+      if constexpr (FUSED) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) acc[N * N + j] = __ffma2_rn(gu, x[j], acc[N * N + j]);
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) acc[N * N + N + i2] = __ffma2_rn(g[i2], f, acc[N * N + N + i2]);
+      }
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) acc[N * N + i2] = __ffma2_rn(g[i2], av, acc[N * N + i2]);
+#pragma unroll
+        for (int j = 0; j < N; ++j) acc[N * N + N + j] = __ffma2_rn(bt, x[j], acc[N * N + N + j]);
+      }
+    }
+    if (gxt) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) stg_words<W>(gxt + j * D + e0, gxo[j]);
+    }
+    if constexpr (FUSED) {
+      if (gft) stg_words<W>(gft + e0, gfo);
+    }
+  }
+}
+
 // ================================================================= forward
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
@@ -410,7 +638,7 @@ __device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
-__global__ void __launch_bounds__(warp_cap(N) * 32, 1)
+__global__ void __launch_bounds__(fwd_warp_cap(N) * 32, 1)
 mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   constexpr int NS = FUSED ? 1 : N;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -431,7 +659,8 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
-    TokParams<P, N, FUSED, PROJ> pr;
+    using Params = std::conditional_t<use_pairs(N), TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
+    Params pr;
     RingCursor cur{c, 0u, c};
     for (int g0 = 0; g0 < ntok; g0 += C) {
       const int Wg = min(C, ntok - g0);
@@ -449,8 +678,13 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
         }
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch, t,
-                                           d0, len, lane);
+        if constexpr (use_pairs(N)) {
+          fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch,
+                                              t, d0, len, lane);
+        } else {
+          fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch,
+                                             t, d0, len, lane);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
         cur.advance(p + 1 < ns ? Wg : C, S);
@@ -568,11 +802,14 @@ __device__ __forceinline__ void bwd_slice(const MixBwdArgs& a, const TokParams<P
   }
 }
 
+__device__ __forceinline__ float phi_of(float v) { return v; }
+__device__ __forceinline__ float phi_of(float2 v) { return v.x; }
+
 // Fold the 32 lanes' partial sums of one token and write its parameter
 // gradients (and grad_v for the projection).
-template <typename P, int N, bool FUSED, bool PROJ>
-__device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
-                                           const float* acc, int64_t t, int lane) {
+template <typename P, int N, bool FUSED, bool PROJ, typename Params>
+__device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const Params& pr, const float* acc, int64_t t,
+                                           int lane) {
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int R = L::kR;
   float v[L::kPad];
@@ -610,7 +847,7 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const TokParams<
         if (j == lane) {
           float ptr = 0.f;
 #pragma unroll
-          for (int i2 = 0; i2 < N; ++i2) ptr = fmaf(pr.phi[i2 * N + j], rho[i2], ptr);
+          for (int i2 = 0; i2 < N; ++i2) ptr = fmaf(phi_of(pr.phi[i2 * N + j]), rho[i2], ptr);
           out = (rho[j] - ptr) + bp[j];
         }
       }
@@ -620,7 +857,7 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const TokParams<
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
-__global__ void __launch_bounds__(warp_cap(N) * 32, 1)
+__global__ void __launch_bounds__(bwd_warp_cap(N) * 32, 1)
 mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
@@ -652,8 +889,11 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
-    TokParams<P, N, FUSED, PROJ> pr;
+    constexpr bool PAIRS = use_pairs(N);
+    using Params = std::conditional_t<PAIRS, TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
+    Params pr;
     float acc[L::kPad];
+    float2 acc2[PAIRS ? L::kAcc : 1];
     RingCursor cur{c, 0u, c};
     for (int g0 = 0; g0 < ntok; g0 += C) {
       const int Wg = min(C, ntok - g0);
@@ -662,6 +902,10 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
       pr.load(a.phi, a.v, a.alpha, a.beta, t);
 #pragma unroll
       for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+      if constexpr (PAIRS) {
+#pragma unroll
+        for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
+      }
       bool done = true;
       for (int p = 0; p < ns; ++p) {
         if (__any_sync(kFull, st.abort)) {
@@ -678,13 +922,22 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         }
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
-                                           geo.pitch, t, d0, len, lane);
+        if constexpr (PAIRS) {
+          bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
+                                              geo.pitch, t, d0, len, lane);
+        } else {
+          bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
+                                             geo.pitch, t, d0, len, lane);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
         cur.advance(p + 1 < ns ? Wg : C, S);
       }
       if (!done) break;
+      if constexpr (PAIRS) {
+#pragma unroll
+        for (int k = 0; k < L::kAcc; ++k) acc[k] = acc2[k].x + acc2[k].y;
+      }
       bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
     }
   }
@@ -726,7 +979,7 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_
   geo.stage_bytes = static_cast<int>(rows * sl * esize);
   int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
   if (tune.stages > 0) stages = std::min(stages, tune.stages);
-  int consumers = std::min(warp_cap(n) - 1, stages - 2);
+  int consumers = std::min(warp_cap(bwd, n) - 1, stages - 2);
   if (tune.warps > 0) consumers = std::min(consumers, tune.warps);
   if (consumers < 1 || stages < 3) return false;
   geo.stages = stages;
