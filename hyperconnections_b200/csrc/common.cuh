@@ -128,6 +128,50 @@ template <typename T, bool VECTOR> struct Chunk {
 };
 
 // ------------------------------------------------------- small parameter rows
+// Loads that the compiler may not repeat: values a thread keeps in registers
+// for a whole token (re-loading them inside the element loops would put an L1
+// round trip in front of every chunk).
+__device__ __forceinline__ float4 ldg_keep_f4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float ldg_keep_f32(const float* p) {
+  float r;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ unsigned short ldg_keep_u16(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+
+template <typename P> __device__ __forceinline__ float ldg_keep_elem(const P* p);
+template <> __device__ __forceinline__ float ldg_keep_elem<float>(const float* p) { return ldg_keep_f32(p); }
+template <> __device__ __forceinline__ float ldg_keep_elem<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __uint_as_float(static_cast<uint32_t>(ldg_keep_u16(p)) << 16);
+}
+template <> __device__ __forceinline__ float ldg_keep_elem<__half>(const __half* p) {
+  return __half2float(__ushort_as_half(ldg_keep_u16(p)));
+}
+
+// K consecutive parameters loaded once into registers (see ldg_keep_f4).
+template <typename P, int K>
+__device__ __forceinline__ void load_params_keep(const P* __restrict__ src, float (&dst)[K]) {
+  if constexpr (sizeof(P) == 4 && (K % 4) == 0) {
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+#pragma unroll
+      for (int k = 0; k < K; k += 4) {
+        const float4 q = ldg_keep_f4(reinterpret_cast<const float*>(src) + k);
+        dst[k] = q.x; dst[k + 1] = q.y; dst[k + 2] = q.z; dst[k + 3] = q.w;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) dst[k] = ldg_keep_elem<P>(src + k);
+}
 // Load K consecutive parameters (converted to fp32). Vector path when the row
 // starts on a 16-byte boundary and K*4 is a multiple of 16 (fp32 params).
 template <typename P, int K>

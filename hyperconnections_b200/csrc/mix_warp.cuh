@@ -322,9 +322,9 @@ struct TokParams {
   float al[FUSED ? N : 1], be[FUSED ? N : 1];
   __device__ __forceinline__ void load(const void* phi_p, const void* v_p, const float* alpha, const float* beta,
                                        int64_t t) {
-    load_params<P, N * N>(static_cast<const P*>(phi_p) + t * (N * N), phi);
+    load_params_keep<P, N * N>(static_cast<const P*>(phi_p) + t * (N * N), phi);
     if constexpr (PROJ) {
-      load_params<P, N>(static_cast<const P*>(v_p) + t * N, vv);
+      load_params_keep<P, N>(static_cast<const P*>(v_p) + t * N, vv);
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         float pv = 0.f;
@@ -334,8 +334,8 @@ struct TokParams {
       }
     }
     if constexpr (FUSED) {
-      load_params<float, N>(alpha + t * N, al);
-      load_params<float, N>(beta + t * N, be);
+      load_params_keep<float, N>(alpha + t * N, al);
+      load_params_keep<float, N>(beta + t * N, be);
     }
   }
 };
@@ -996,7 +996,10 @@ inline int warp_prepare(KernelT* kernel, int smem_bytes) {
   return HC_OK;
 }
 
-constexpr int kWarpW = 2;  // 32-bit words per lane access (8-byte accesses)
+// 32-bit words per lane access: 16-byte accesses for the forward at n <= 4,
+// 8-byte accesses elsewhere (register budget).
+constexpr int fwd_lane_words(int n) { return n <= 4 ? 4 : 2; }
+constexpr int kWarpW = 2;
 
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cudaStream_t s) {
@@ -1004,7 +1007,7 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cud
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
-    auto* k = mix_fwd_warp_kernel<T, P, NN, FUSED, PROJ, kWarpW>;       \
+    auto* k = mix_fwd_warp_kernel<T, P, NN, FUSED, PROJ, fwd_lane_words(NN)>;       \
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;            \
     k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);                  \
     break;                                                              \
