@@ -162,8 +162,9 @@ __device__ __forceinline__ void stg_words(void* p, const uint32_t* w) {
 struct WarpGeometry {
   int consumers;    // consumer warps per CTA (one producer warp besides)
   int stages;       // stages of the CTA's ring
+  int tpi;          // tokens per item (several small tokens share a stage)
   int sl;           // elements per slice
-  int ns;           // slices per token
+  int ns;           // slices per token (ns > 1 only with tpi == 1)
   int pitch;        // shared-memory row pitch (elements)
   int stage_bytes;  // rows * pitch * element size
   int grid;         // CTAs
@@ -177,29 +178,30 @@ constexpr int fwd_warp_cap(int n) { return n <= 4 ? 16 : 8; }
 constexpr int bwd_warp_cap(int n) { return n <= 4 ? 12 : 8; }
 constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap(n) : fwd_warp_cap(n); }
 
-// Issue the bulk copies of one token-slice into a stage (producer lane).
+// Issue the bulk copies of one item (cnt consecutive tokens, or one slice of
+// one token) into a stage. Stage layout: [tensor][token][row][pitch].
 template <typename T, int NIN>
 __device__ __forceinline__ void ring_issue(const WarpGeometry& geo, int64_t D, uint8_t* stage, uint64_t* bar,
-                                           int64_t t, int p, const void* const* base, const int* rows) {
+                                           int64_t t0, int cnt, int p, const void* const* base, const int* rows) {
   constexpr int es = sizeof(T);
   const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
   const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
   int rtot = 0;
 #pragma unroll
   for (int k = 0; k < NIN; ++k) rtot += rows[k];
-  mbar_expect_tx(bar, static_cast<uint32_t>(rtot * len * es));
+  mbar_expect_tx(bar, static_cast<uint32_t>(cnt * rtot * len * es));
   uint8_t* dst = stage;
 #pragma unroll
   for (int k = 0; k < NIN; ++k) {
-    const T* src = static_cast<const T*>(base[k]) + t * rows[k] * D;
-    if (geo.ns == 1) {
-      bulk_g2s(dst, src, static_cast<uint32_t>(rows[k] * D * es), bar);
+    const T* src = static_cast<const T*>(base[k]) + t0 * rows[k] * D;
+    if (geo.ns == 1) {  // cnt whole tokens: contiguous in HBM
+      bulk_g2s(dst, src, static_cast<uint32_t>(cnt * rows[k] * D * es), bar);
     } else {
       for (int r = 0; r < rows[k]; ++r)
         bulk_g2s(dst + static_cast<size_t>(r) * geo.pitch * es, src + r * D + d0, static_cast<uint32_t>(len * es),
                  bar);
     }
-    dst += static_cast<size_t>(rows[k]) * geo.pitch * es;
+    dst += static_cast<size_t>(geo.tpi) * rows[k] * geo.pitch * es;
   }
 }
 
@@ -207,14 +209,6 @@ __device__ __forceinline__ void ring_issue(const WarpGeometry& geo, int64_t D, u
 struct RingState {
   uint64_t full[kRingMaxStages];
   uint64_t empty[kRingMaxStages];
-  // Item index of the fill most recently started in each stage. A stage is
-  // shared by items of different consumers in successive rounds, and a parity
-  // wait can only tell adjacent phases apart: a consumer that reached item k
-  // while item k - S (another consumer's) was still landing would see the
-  // wrong phase as complete. Consumers therefore wait for tag == k first.
-  volatile long long tag[kRingMaxStages];
-  uint32_t last_parity[kRingMaxStages];  // parity of the last fill issued into each stage
-  int issued[kRingMaxStages];
   volatile int abort;
 };
 
@@ -223,9 +217,6 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&st.full[s], 1);
       mbar_init(&st.empty[s], 1);
-      st.tag[s] = -1;
-      st.issued[s] = 0;
-      st.last_parity[s] = 0;
     }
     st.abort = 0;
     fence_mbar_init();
@@ -233,35 +224,34 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
   __syncthreads();
 }
 
-// Producer loop (one lane): fills stages in ring order. Item order within a
-// group of C tokens: slice-major, so consecutive items of one consumer are C
-// apart and each consumer has its next slice in flight.
+// Producer loop (one lane). Work is cut into "units" (tpi consecutive tokens)
+// dealt round-robin to the C consumers; units are issued in groups of C,
+// slice-major inside a group, so consecutive items of one consumer are at most
+// C apart and every consumer has its next item in flight. Item k goes to stage
+// k mod S; the producer reuses a stage once the consumer of item k - S has
+// released it.
 template <typename T, int NIN>
 __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& geo, uint8_t* smem, int64_t D,
-                                             int64_t t_begin, int ntok, const void* const* base, const int* rows) {
+                                             int64_t t_begin, int ntok, int nunits, const void* const* base,
+                                             const int* rows) {
   const int S = geo.stages, C = geo.consumers;
   int s = 0;
   uint32_t ph = 0;
   int64_t k = 0;
-  for (int g0 = 0; g0 < ntok; g0 += C) {
-    const int Wg = min(C, ntok - g0);
+  for (int g0 = 0; g0 < nunits; g0 += C) {
+    const int Wg = min(C, nunits - g0);
     for (int p = 0; p < geo.ns; ++p) {
       for (int w = 0; w < Wg; ++w) {
         if (st.abort) return;
-        if (k >= S) {  // wait until the consumer of item k - S released this stage
-          if (!warp_wait(&st.empty[s], ph ^ 1u)) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
-            st.abort = 1;
-            return;
-          }
-          fence_proxy_async_smem();
+        if (k >= S && !warp_wait(&st.empty[s], ph ^ 1u)) {
+          atomicAdd(&g_mix_wait_timeouts, 1u);
+          st.abort = 1;
+          return;
         }
-        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s], t_begin + g0 + w, p,
-                           base, rows);
-        __threadfence_block();  // the arrive.expect_tx above is visible before the tag
-        st.tag[s] = k;
-        st.issued[s] = 1;
-        st.last_parity[s] = ph;
+        const int u = g0 + w;
+        const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
+                           t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
         ++k;
         if (++s == S) {
           s = 0;
@@ -274,19 +264,20 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
 
 // Before the CTA exits: wait (bounded) for the last fill of every stage, so
 // that no copy is still in flight (immediate in a normal run).
-__device__ __forceinline__ void ring_drain(RingState& st, int stages) {
+__device__ __forceinline__ void ring_drain(RingState& st, int stages, int64_t nitems) {
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int s = 0; s < stages; ++s)
-      if (st.issued[s]) warp_wait(&st.full[s], st.last_parity[s]);
+    for (int s = 0; s < stages && s < nitems; ++s) {
+      const int64_t last = s + ((nitems - 1 - s) / stages) * stages;
+      warp_wait(&st.full[s], static_cast<uint32_t>((last / stages) & 1));
+    }
 }
 
-// Consumer-side cursor over the ring: item k = g0*ns + p*Wg + c; stage and
-// parity advance by the distance to the consumer's next item.
+// Consumer-side cursor over the ring: item index k, its stage and parity.
 struct RingCursor {
   int s;
   uint32_t ph;
-  long long k;  // item index
+  long long k;
   __device__ __forceinline__ void advance(int delta, int S) {
     k += delta;
     s += delta;
@@ -297,19 +288,15 @@ struct RingCursor {
   }
 };
 
-// Consumer wait for its item: first until the producer has started this
-// item's fill (tag), then on the fill's phase. Bounded; warp-uniform result.
-__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur) {
-  bool ok = false;
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (st.tag[cur.s] == cur.k) {
-      ok = true;
-      break;
-    }
-    if (st.abort) break;
-    __nanosleep(32);
-  }
-  __threadfence_block();
+// Consumer wait for its item k (round r on stage s). A stage is shared by items
+// of different consumers in successive rounds, and a parity wait only tells
+// adjacent phases apart, so the consumer first waits for the release of the
+// stage's previous occupant (item k - S, round r - 1, exact because item k - 2S
+// is necessarily released already) and only then for its own fill (round r).
+// Bounded; warp-uniform result.
+__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur, int S) {
+  bool ok = true;
+  if (cur.k >= S) ok = warp_wait(&st.empty[cur.s], cur.ph ^ 1u);
   if (ok) ok = warp_wait(&st.full[cur.s], cur.ph);
   return __all_sync(kFull, ok);
 }
@@ -414,7 +401,8 @@ struct TokParams2 {
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void fwd_slice2(const MixFwdArgs& a, const TokParams2<P, N, FUSED, PROJ>& pr,
-                                           const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len, int lane) {
+                                           const uint8_t* xsb, const uint8_t* ssb, int pitch, int64_t t, int64_t d0,
+                                           int len, int lane) {
   using IO = PairIO<T>;
   constexpr int K = Word<T>::K;
   constexpr int WP = IO::WORDS;
@@ -428,12 +416,12 @@ __device__ __forceinline__ void fwd_slice2(const MixFwdArgs& a, const TokParams2
   T* ut = FUSED ? static_cast<T*>(a.u) + t * D + d0 : nullptr;
   const float2 zero = make_float2(0.f, 0.f);
   for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> xw[N], sw[NS];
 #pragma unroll
-    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(q + j * rowb);
+    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(xsb + eo + j * rowb);
 #pragma unroll
-    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(q + (N + i2) * rowb);
+    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(ssb + eo + i2 * rowb);
     uint32_t ow[N][W], uw[W];
 #pragma unroll
     for (int w = 0; w < W; w += WP) {
@@ -475,8 +463,9 @@ __device__ __forceinline__ void fwd_slice2(const MixFwdArgs& a, const TokParams2
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void bwd_slice2(const MixBwdArgs& a, const TokParams2<P, N, FUSED, PROJ>& pr,
-                                           float2* acc, const uint8_t* sb, int pitch, int64_t t, int64_t d0,
-                                           int len, int lane) {
+                                           float2* acc, const uint8_t* gsb, const uint8_t* xsb, const uint8_t* usb,
+                                           const uint8_t* fsb, int pitch, int64_t t, int64_t d0, int len,
+                                           int lane) {
   using IO = PairIO<T>;
   constexpr int K = Word<T>::K;
   constexpr int WP = IO::WORDS;
@@ -489,15 +478,15 @@ __device__ __forceinline__ void bwd_slice2(const MixBwdArgs& a, const TokParams2
   T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
   const float2 zero = make_float2(0.f, 0.f);
   for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> gwr[N], xwr[N], uwr, fwr;
 #pragma unroll
-    for (int r = 0; r < N; ++r) gwr[r] = lds_words<W>(q + r * rowb);
+    for (int r = 0; r < N; ++r) gwr[r] = lds_words<W>(gsb + eo + r * rowb);
 #pragma unroll
-    for (int r = 0; r < N; ++r) xwr[r] = lds_words<W>(q + (N + r) * rowb);
+    for (int r = 0; r < N; ++r) xwr[r] = lds_words<W>(xsb + eo + r * rowb);
     if constexpr (FUSED) {
-      uwr = lds_words<W>(q + (2 * N) * rowb);
-      fwr = lds_words<W>(q + (2 * N + 1) * rowb);
+      uwr = lds_words<W>(usb + eo);
+      fwr = lds_words<W>(fsb + eo);
     }
     uint32_t gxo[N][W], gfo[W];
 #pragma unroll
@@ -566,7 +555,8 @@ __device__ __forceinline__ void bwd_slice2(const MixBwdArgs& a, const TokParams2
 // ================================================================= forward
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
-                                          const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len, int lane) {
+                                          const uint8_t* xsb, const uint8_t* ssb, int pitch, int64_t t, int64_t d0,
+                                          int len, int lane) {
   using Wd = Word<T>;
   constexpr int K = Wd::K;
   constexpr int NS = FUSED ? 1 : N;
@@ -577,12 +567,12 @@ __device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P
   T* ot = static_cast<T*>(a.out) + t * N * D + d0;
   T* ut = FUSED ? static_cast<T*>(a.u) + t * D + d0 : nullptr;
   for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> xw[N], sw[NS];
 #pragma unroll
-    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(q + j * rowb);
+    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(xsb + eo + j * rowb);
 #pragma unroll
-    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(q + (N + i2) * rowb);
+    for (int i2 = 0; i2 < NS; ++i2) sw[i2] = lds_words<W>(ssb + eo + i2 * rowb);
     uint32_t ow[N][W], uw[W];
 #pragma unroll
     for (int w = 0; w < W; ++w) {
@@ -641,6 +631,7 @@ template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __global__ void __launch_bounds__(fwd_warp_cap(N) * 32, 1)
 mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   constexpr int NS = FUSED ? 1 : N;
+  constexpr int es = sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
   ring_init(st, geo.stages);
@@ -648,58 +639,69 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
   const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
+  const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
+  const uint32_t xregion = static_cast<uint32_t>(geo.tpi) * N * rowb;  // bytes of the x rows of a stage
 
   if (warp == 0) {
     if (lane == 0) {
       const void* base[2] = {a.x, a.src};
       const int rows[2] = {N, NS};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, base, rows);
+      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
     using Params = std::conditional_t<use_pairs(N), TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
     Params pr;
     RingCursor cur{c, 0u, c};
-    for (int g0 = 0; g0 < ntok; g0 += C) {
-      const int Wg = min(C, ntok - g0);
+    for (int g0 = 0; g0 < nunits; g0 += C) {
+      const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
-      const int64_t t = t_begin + g0 + c;
-      pr.load(a.phi, a.v, a.alpha, a.beta, t);
+      const int u = g0 + c;
+      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
+      bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort)) break;
-        if (!ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, S)) {
           if (lane == 0 && !st.abort) {
             atomicAdd(&g_mix_wait_timeouts, 1u);
             st.abort = 1;
           }
+          ok = false;
           break;
         }
+        const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        if constexpr (use_pairs(N)) {
-          fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch,
-                                              t, d0, len, lane);
-        } else {
-          fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, smem + static_cast<size_t>(cur.s) * geo.stage_bytes, geo.pitch,
-                                             t, d0, len, lane);
+        for (int tt = 0; tt < cnt; ++tt) {
+          const int64_t t = t0 + tt;
+          if (p == 0 && tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
+          const uint8_t* xs = sb + tt * N * rowb;
+          const uint8_t* ss = sb + xregion + tt * NS * rowb;
+          if constexpr (use_pairs(N)) {
+            fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+          } else {
+            fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
         cur.advance(p + 1 < ns ? Wg : C, S);
       }
-      if (__any_sync(kFull, st.abort)) break;
+      if (!ok) break;
     }
   }
-  ring_drain(st, S);
+  ring_drain(st, S, static_cast<int64_t>(nunits) * ns);
 }
 
 // ================================================================= backward
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void bwd_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
-                                          float* acc, const uint8_t* sb, int pitch, int64_t t, int64_t d0, int len,
-                                          int lane) {
+                                          float* acc, const uint8_t* gsb, const uint8_t* xsb, const uint8_t* usb,
+                                          const uint8_t* fsb, int pitch, int64_t t, int64_t d0, int len, int lane) {
   using Wd = Word<T>;
   constexpr int K = Wd::K;
   constexpr int es = sizeof(T);
@@ -709,15 +711,15 @@ __device__ __forceinline__ void bwd_slice(const MixBwdArgs& a, const TokParams<P
   T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
   T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
   for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
-    const uint8_t* q = sb + static_cast<uint32_t>(e0) * es;
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> gw_[N], xw[N], uw, fw;
 #pragma unroll
-    for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(q + r * rowb);
+    for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(gsb + eo + r * rowb);
 #pragma unroll
-    for (int r = 0; r < N; ++r) xw[r] = lds_words<W>(q + (N + r) * rowb);
+    for (int r = 0; r < N; ++r) xw[r] = lds_words<W>(xsb + eo + r * rowb);
     if constexpr (FUSED) {
-      uw = lds_words<W>(q + (2 * N) * rowb);
-      fw = lds_words<W>(q + (2 * N + 1) * rowb);
+      uw = lds_words<W>(usb + eo);
+      fw = lds_words<W>(fsb + eo);
     }
     uint32_t gxo[N][W], gfo[W];
 #pragma unroll
@@ -861,6 +863,7 @@ __global__ void __launch_bounds__(bwd_warp_cap(N) * 32, 1)
 mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
+  constexpr int es = sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
   ring_init(st, geo.stages);
@@ -868,8 +871,12 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
   const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
+  const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
+  const uint32_t nreg = static_cast<uint32_t>(geo.tpi) * N * rowb;  // bytes of n rows x tpi tokens
+  const uint32_t oreg = static_cast<uint32_t>(geo.tpi) * rowb;      // bytes of 1 row x tpi tokens
 
   if (warp == 0) {
     if (lane == 0) {
@@ -885,7 +892,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         rows[2] = 1;
         rows[3] = 1;
       }
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, base, rows);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -895,53 +902,62 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
     float acc[L::kPad];
     float2 acc2[PAIRS ? L::kAcc : 1];
     RingCursor cur{c, 0u, c};
-    for (int g0 = 0; g0 < ntok; g0 += C) {
-      const int Wg = min(C, ntok - g0);
+    for (int g0 = 0; g0 < nunits; g0 += C) {
+      const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
-      const int64_t t = t_begin + g0 + c;
-      pr.load(a.phi, a.v, a.alpha, a.beta, t);
-#pragma unroll
-      for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
-      if constexpr (PAIRS) {
-#pragma unroll
-        for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
-      }
-      bool done = true;
+      const int u = g0 + c;
+      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
+      bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort)) {
-          done = false;
-          break;
-        }
-        if (!ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, S)) {
           if (lane == 0 && !st.abort) {
             atomicAdd(&g_mix_wait_timeouts, 1u);
             st.abort = 1;
           }
-          done = false;
+          ok = false;
           break;
         }
+        const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        if constexpr (PAIRS) {
-          bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
-                                              geo.pitch, t, d0, len, lane);
-        } else {
-          bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, smem + static_cast<size_t>(cur.s) * geo.stage_bytes,
-                                             geo.pitch, t, d0, len, lane);
+        for (int tt = 0; tt < cnt; ++tt) {
+          const int64_t t = t0 + tt;
+          if (p == 0) {
+            if (tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
+#pragma unroll
+            for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+            if constexpr (PAIRS) {
+#pragma unroll
+              for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
+            }
+          }
+          const uint8_t* gs = sb + tt * N * rowb;
+          const uint8_t* xs = sb + nreg + tt * N * rowb;
+          const uint8_t* us = sb + 2 * nreg + tt * rowb;
+          const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
+          if constexpr (PAIRS) {
+            bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
+          } else {
+            bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
+          }
+          if (p == ns - 1) {  // token complete (tpi > 1 only with ns == 1)
+            if constexpr (PAIRS) {
+#pragma unroll
+              for (int k = 0; k < L::kAcc; ++k) acc[k] = acc2[k].x + acc2[k].y;
+            }
+            bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
         cur.advance(p + 1 < ns ? Wg : C, S);
       }
-      if (!done) break;
-      if constexpr (PAIRS) {
-#pragma unroll
-        for (int k = 0; k < L::kAcc; ++k) acc[k] = acc2[k].x + acc2[k].y;
-      }
-      bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
+      if (!ok) break;
     }
   }
-  ring_drain(st, S);
+  ring_drain(st, S, static_cast<int64_t>(nunits) * ns);
 }
 
 // ================================================================= host side
@@ -952,7 +968,7 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 
 // Tuning knobs (0 = automatic), set through hc_set_mix_tuning().
 struct WarpTuning {
-  int stage_bytes;  // largest stage before a token is cut into slices
+  int stage_bytes;  // target bytes of an item of several small tokens
   int stages;       // stages of the ring
   int warps;        // consumer warps per CTA
 };
@@ -960,23 +976,32 @@ WarpTuning& warp_tuning();
 
 // Geometry of the ring; false when the shape does not fit it.
 // Requires D % (16 / esize) == 0 and 16-byte aligned stream bases.
+//   * a token whose rows exceed max_stage is cut into slices (one bulk copy
+//     per row slice);
+//   * tokens smaller than the item target are grouped, tpi per item, so that
+//     one bulk copy per tensor moves several tokens.
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
                           int num_sms) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
   const WarpTuning tune = warp_tuning();
   const int rows = warp_rows(bwd, fused, n);
   const int budget = 200 * 1024;
-  const int64_t max_stage = tune.stage_bytes > 0 ? tune.stage_bytes : 24 * 1024;
+  const int64_t max_stage = 24 * 1024;
+  const int64_t item_target = tune.stage_bytes > 0 ? tune.stage_bytes : 12 * 1024;
+  const int64_t tok_bytes = static_cast<int64_t>(rows) * D * esize;
   int64_t sl = D;
-  if (static_cast<int64_t>(rows) * D * esize > max_stage) {
-    const int64_t slice_target = tune.stage_bytes > 0 ? tune.stage_bytes : 16 * 1024;
-    sl = std::max<int64_t>(64, (slice_target / (rows * esize)) / 64 * 64);
+  int tpi = 1;
+  if (tok_bytes > max_stage) {
+    sl = std::max<int64_t>(64, ((16 * 1024) / (rows * esize)) / 64 * 64);
     if (sl >= D) sl = D;
+  } else if (tok_bytes < item_target) {
+    tpi = static_cast<int>(std::min<int64_t>(8, item_target / tok_bytes));
   }
+  geo.tpi = tpi;
   geo.sl = static_cast<int>(sl);
   geo.ns = static_cast<int>((D + sl - 1) / sl);
   geo.pitch = geo.sl;
-  geo.stage_bytes = static_cast<int>(rows * sl * esize);
+  geo.stage_bytes = static_cast<int>(tpi * rows * sl * esize);
   int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
   if (tune.stages > 0) stages = std::min(stages, tune.stages);
   int consumers = std::min(warp_cap(bwd, n) - 1, stages - 2);
