@@ -209,6 +209,14 @@ __device__ __forceinline__ void ring_issue(const WarpGeometry& geo, int64_t D, u
 struct RingState {
   uint64_t full[kRingMaxStages];
   uint64_t empty[kRingMaxStages];
+  // Item index of the fill most recently started in each stage. A stage is
+  // shared by items of different consumers in successive rounds, and a parity
+  // wait can only tell adjacent phases apart: a consumer that reached item k
+  // while item k - S (another consumer's) was still landing would see the
+  // wrong phase as complete. Consumers therefore wait for tag == k first.
+  volatile long long tag[kRingMaxStages];
+  uint32_t last_parity[kRingMaxStages];
+  int issued[kRingMaxStages];
   volatile int abort;
 };
 
@@ -217,6 +225,9 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&st.full[s], 1);
       mbar_init(&st.empty[s], 1);
+      st.tag[s] = -1;
+      st.issued[s] = 0;
+      st.last_parity[s] = 0;
     }
     st.abort = 0;
     fence_mbar_init();
@@ -243,15 +254,22 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
     for (int p = 0; p < geo.ns; ++p) {
       for (int w = 0; w < Wg; ++w) {
         if (st.abort) return;
-        if (k >= S && !warp_wait(&st.empty[s], ph ^ 1u)) {
-          atomicAdd(&g_mix_wait_timeouts, 1u);
-          st.abort = 1;
-          return;
+        if (k >= S) {
+          if (!warp_wait(&st.empty[s], ph ^ 1u)) {
+            atomicAdd(&g_mix_wait_timeouts, 1u);
+            st.abort = 1;
+            return;
+          }
+          fence_proxy_async_smem();
         }
         const int u = g0 + w;
         const int cnt = min(geo.tpi, ntok - u * geo.tpi);
         ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
                            t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
+        __threadfence_block();  // the arrive.expect_tx above is visible before the tag
+        st.tag[s] = k;
+        st.issued[s] = 1;
+        st.last_parity[s] = ph;
         ++k;
         if (++s == S) {
           s = 0;
@@ -263,14 +281,14 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
 }
 
 // Before the CTA exits: wait (bounded) for the last fill of every stage, so
-// that no copy is still in flight (immediate in a normal run).
-__device__ __forceinline__ void ring_drain(RingState& st, int stages, int64_t nitems) {
+// that no copy is still in flight (immediate in a normal run). The producer
+// records each stage's last parity: computing it here would take two 64-bit
+// divisions per stage on one thread, microseconds at the tail of every CTA.
+__device__ __forceinline__ void ring_drain(RingState& st, int stages) {
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int s = 0; s < stages && s < nitems; ++s) {
-      const int64_t last = s + ((nitems - 1 - s) / stages) * stages;
-      warp_wait(&st.full[s], static_cast<uint32_t>((last / stages) & 1));
-    }
+    for (int s = 0; s < stages; ++s)
+      if (st.issued[s]) warp_wait(&st.full[s], st.last_parity[s]);
 }
 
 // Consumer-side cursor over the ring: item index k, its stage and parity.
@@ -288,15 +306,19 @@ struct RingCursor {
   }
 };
 
-// Consumer wait for its item k (round r on stage s). A stage is shared by items
-// of different consumers in successive rounds, and a parity wait only tells
-// adjacent phases apart, so the consumer first waits for the release of the
-// stage's previous occupant (item k - S, round r - 1, exact because item k - 2S
-// is necessarily released already) and only then for its own fill (round r).
-// Bounded; warp-uniform result.
-__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur, int S) {
-  bool ok = true;
-  if (cur.k >= S) ok = warp_wait(&st.empty[cur.s], cur.ph ^ 1u);
+// Consumer wait for its item: first until the producer has started this
+// item's fill (tag), then on the fill's phase. Bounded; warp-uniform result.
+__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur) {
+  bool ok = false;
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (st.tag[cur.s] == cur.k) {
+      ok = true;
+      break;
+    }
+    if (st.abort) break;
+    __nanosleep(32);
+  }
+  __threadfence_block();
   if (ok) ok = warp_wait(&st.full[cur.s], cur.ph);
   return __all_sync(kFull, ok);
 }
@@ -644,6 +666,7 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
   const uint32_t xregion = static_cast<uint32_t>(geo.tpi) * N * rowb;  // bytes of the x rows of a stage
+  const bool single = geo.tpi == 1;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -665,7 +688,7 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, S)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
           if (lane == 0 && !st.abort) {
             atomicAdd(&g_mix_wait_timeouts, 1u);
             st.abort = 1;
@@ -676,15 +699,23 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
         const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        for (int tt = 0; tt < cnt; ++tt) {
-          const int64_t t = t0 + tt;
-          if (p == 0 && tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
-          const uint8_t* xs = sb + tt * N * rowb;
-          const uint8_t* ss = sb + xregion + tt * NS * rowb;
+        if (single) {  // one token (or slice) per item: the common, hottest path
           if constexpr (use_pairs(N)) {
-            fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+            fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, sb, sb + N * rowb, geo.pitch, t0, d0, len, lane);
           } else {
-            fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+            fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, sb, sb + N * rowb, geo.pitch, t0, d0, len, lane);
+          }
+        } else {
+          for (int tt = 0; tt < cnt; ++tt) {
+            const int64_t t = t0 + tt;
+            if (tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
+            const uint8_t* xs = sb + tt * N * rowb;
+            const uint8_t* ss = sb + xregion + tt * NS * rowb;
+            if constexpr (use_pairs(N)) {
+              fwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+            } else {
+              fwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, xs, ss, geo.pitch, t, d0, len, lane);
+            }
           }
         }
         __syncwarp();
@@ -694,7 +725,7 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
       if (!ok) break;
     }
   }
-  ring_drain(st, S, static_cast<int64_t>(nunits) * ns);
+  ring_drain(st, S);
 }
 
 // ================================================================= backward
@@ -877,6 +908,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
   const uint32_t nreg = static_cast<uint32_t>(geo.tpi) * N * rowb;  // bytes of n rows x tpi tokens
   const uint32_t oreg = static_cast<uint32_t>(geo.tpi) * rowb;      // bytes of 1 row x tpi tokens
+  const bool single = geo.tpi == 1;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -911,7 +943,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, S)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
           if (lane == 0 && !st.abort) {
             atomicAdd(&g_mix_wait_timeouts, 1u);
             st.abort = 1;
@@ -922,8 +954,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
-        for (int tt = 0; tt < cnt; ++tt) {
-          const int64_t t = t0 + tt;
+        auto token = [&](int tt, int64_t t) {
           if (p == 0) {
             if (tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
 #pragma unroll
@@ -949,6 +980,11 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
             }
             bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
           }
+        };
+        if (single) {
+          token(0, t0);
+        } else {
+          for (int tt = 0; tt < cnt; ++tt) token(tt, t0 + tt);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
@@ -957,7 +993,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
       if (!ok) break;
     }
   }
-  ring_drain(st, S, static_cast<int64_t>(nunits) * ns);
+  ring_drain(st, S);
 }
 
 // ================================================================= host side
