@@ -236,8 +236,8 @@ class FusedRunner:
         self._check(rc, "hc_fused_bwd")
 
 
-def time_fused(device, steps, warmup, world):
-    runner = FusedRunner(device)
+def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK):
+    runner = FusedRunner(device, T=T, n=n, D=D)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for _ in range(warmup):
@@ -265,11 +265,61 @@ def time_fused(device, steps, warmup, world):
     return {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t1), "launches": 2 * steps}
 
 
-def time_expm(device, steps, warmup):
+class ExpmRunner:
+    """Direct C-ABI launches of the batched T18 expm forward and backward
+    (global scaling, the reference's semantics) on resident device buffers."""
+
+    def __init__(self, device, B=EXPM_BATCH, n=EXPM_N, seed=0):
+        from hyperconnections_b200 import _lib
+
+        self.lib = _lib.lib()
+        self.B, self.n = B, n
+        self.A, self.G = (t.to(device) for t in expm_workload(B, n, seed=seed))
+        self.E = torch.empty_like(self.A)
+        self.dA = torch.empty_like(self.A)
+        self.words = max(1, self.lib.hc_expm_t18_scratch_words(B, n))
+        self.scratch = torch.empty(self.words, dtype=torch.float32, device=device)
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        self._check = _lib.check
+
+    def fwd(self):
+        rc = self.lib.hc_expm_t18_fwd(self.A.data_ptr(), self.E.data_ptr(), self.B, self.n,
+                                      self.scratch.data_ptr(), self.words, 0, self.stream)
+        self._check(rc, "hc_expm_t18_fwd")
+
+    def bwd(self):
+        rc = self.lib.hc_expm_t18_bwd(self.A.data_ptr(), self.G.data_ptr(), self.dA.data_ptr(), self.B, self.n,
+                                      self.scratch.data_ptr(), self.words, 0, self.stream)
+        self._check(rc, "hc_expm_t18_bwd")
+
+
+def time_expm(device, steps, warmup, B=EXPM_BATCH, n=EXPM_N):
+    """Device time of one expm forward + backward over B resident matrices
+    (C-ABI launches), L2 flushed between steps; ms per step."""
+    runner = ExpmRunner(device, B, n)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    for _ in range(warmup):
+        runner.fwd()
+        runner.bwd()
+    torch.cuda.synchronize(device)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(float(i))
+        evs[i][0].record()
+        runner.fwd()
+        runner.bwd()
+        evs[i][1].record()
+    torch.cuda.synchronize(device)
+    del flush
+    return [e[0].elapsed_time(e[1]) for e in evs]
+
+
+def time_expm_api(device, steps, warmup):
+    """The same work through the public API (``expm_t18`` + autograd), which
+    adds the host cost of autograd and of allocating outputs and scratch."""
     from hyperconnections_b200.ops import expm_t18
 
     A, G = (t.to(device) for t in expm_workload(EXPM_BATCH, EXPM_N))
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def step():
         a = A.detach().requires_grad_(True)
@@ -280,51 +330,66 @@ def time_expm(device, steps, warmup):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize(device)
-    ms = []
-    for i in range(steps):
-        flush.fill_(float(i))
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
         step()
-        e1.record()
-        torch.cuda.synchronize(device)
-        ms.append(e0.elapsed_time(e1))
-    del flush
-    return ms
+    e1.record()
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1) / steps
 
 
 def time_e2e(device, steps, warmup):
     """The same fused step through the public API (autograd) with inputs in
     pinned host memory: every step copies its inputs host->device and reads
-    every output back device->host."""
+    every output back device->host.
+
+    Three streams, as a training input pipeline would run it: the upload of
+    step i+1 (copy stream) overlaps the download of step i (download
+    stream), so both PCIe directions are busy at once; the kernels run on the
+    current stream between them, ordered by events."""
     from hyperconnections_b200.ops import stream_mix_fused
 
     host = [t.pin_memory() for t in fused_workload(TOKENS, N_STREAMS, BLOCK, seed=1)]
     h2d = sum(t.numel() * t.element_size() for t in host)
+    comp = torch.cuda.current_stream(device)
+    up = torch.cuda.Stream(device)
+    down = torch.cuda.Stream(device)
     outs_host = None
 
     def step():
         nonlocal outs_host
-        x, f, H, a, b, g_u, g_x = (t.to(device, non_blocking=True) for t in host)
+        with torch.cuda.stream(up):
+            dev = [t.to(device, non_blocking=True) for t in host]
+        comp.wait_stream(up)
+        for t in dev:
+            t.record_stream(comp)
+        x, f, H, a, b, g_u, g_x = dev
         leaves = [t.requires_grad_(True) for t in (x, f, H, a, b)]
         u, x_out = stream_mix_fused(*leaves)
         torch.autograd.backward([u, x_out], [g_u, g_x])
-        outs = [u, x_out] + [t.grad for t in leaves]
+        outs = [u.detach(), x_out.detach()] + [t.grad for t in leaves]
         if outs_host is None:
             outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
-        for dst, src in zip(outs_host, outs):
-            dst.copy_(src.detach(), non_blocking=True)
+        down.wait_stream(comp)
+        with torch.cuda.stream(down):
+            for dst, src in zip(outs_host, outs):
+                src.record_stream(down)
+                dst.copy_(src, non_blocking=True)
         return sum(o.numel() * o.element_size() for o in outs)
 
     for _ in range(warmup):
         step()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(comp)
+    up.wait_stream(comp)
+    down.wait_stream(comp)
     d2h = 0
     for _ in range(steps):
         d2h = step()
-    e1.record()
+    comp.wait_stream(down)
+    e1.record(comp)
     torch.cuda.synchronize(device)
     return e0.elapsed_time(e1) / steps, h2d, d2h
 
@@ -446,6 +511,7 @@ def run_b200(args):
     expm_step = float(np.mean(expm_ms))
     expm_step_max = max_over_ranks(expm_step, world, device)
     expm_rate = world * EXPM_BATCH / (expm_step_max * 1e-3)
+    expm_api_ms = max_over_ranks(time_expm_api(device, 20, 3), world, device)
 
     e2e_ms, h2d, d2h = time_e2e(device, max(3, min(args.steps, 10)), 2)
     e2e_ms_max = max_over_ranks(e2e_ms, world, device)
@@ -480,10 +546,14 @@ def run_b200(args):
             },
             "expm": {"metric": "batched expm fwd+bwd matrices/s", "value": expm_rate, "unit": "matrices/s",
                      "ms_per_step": expm_step_max, "batch": EXPM_BATCH, "n": EXPM_N,
-                     "scaling": "global (reference semantics)"},
+                     "scaling": "global (reference semantics)",
+                     "api": {"value": world * EXPM_BATCH / (expm_api_ms * 1e-3), "unit": "matrices/s",
+                             "ms_per_step": expm_api_ms,
+                             "path": "hyperconnections_b200.ops.expm_t18 + autograd (host-bound)"}},
             "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_ms_max,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "hyperconnections_b200.ops.stream_mix_fused + autograd, pinned host buffers"},
+                    "path": "hyperconnections_b200.ops.stream_mix_fused + autograd, pinned host buffers, "
+                            "upload of step i+1 overlapping download of step i"},
             "gpu_launches": res["launches"],
             "clocks": clocks,
         }
@@ -510,6 +580,138 @@ def run_b200(args):
         torch.distributed.destroy_process_group()
 
 
+def rw_bytes(T: int, n: int, m: int, D: int, proj: bool, esize: int = 2) -> dict:
+    """Algorithmic bytes (each tensor once) of the read and mix-write halves."""
+    return {
+        "read_fwd": T * ((n + m) * D * esize + m * n * 4),
+        "read_bwd": T * ((m + 2 * n) * D * esize + 2 * m * n * 4),
+        "mix_write_fwd": T * ((2 * n + m) * D * esize + (n * n + n * m + (n if proj else 0)) * 4),
+        "mix_write_bwd": T * ((3 * n + 2 * m) * D * esize + (2 * (n * n + n * m) + (2 * n if proj else 0)) * 4),
+    }
+
+
+class RwRunner:
+    """Direct C-ABI launches of the read and mix-write kernels (two-phase
+    layer: read before the wrapped module, mix + write after it)."""
+
+    def __init__(self, device, T, n, m, D, proj, seed=0):
+        from hyperconnections_b200 import _lib
+
+        self.lib, self._check = _lib.lib(), _lib.check
+        self.T, self.n, self.m, self.D = T, n, m, D
+        g = torch.Generator().manual_seed(seed)
+        bf = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).to(device)  # noqa: E731
+        self.x, self.f, self.g_u, self.g_x = bf(T, n, D), bf(T, m, D), bf(T, m, D), bf(T, n, D)
+        self.R = torch.rand(T, m, n, generator=g).to(device)
+        self.W = torch.rand(T, n, m, generator=g).to(device)
+        self.H = torch.rand(T, n, n, generator=g).to(device)
+        self.v = torch.rand(T, n, generator=g).to(device) if proj else None
+        self.u = torch.empty(T, m, D, dtype=torch.bfloat16, device=device)
+        self.out = torch.empty_like(self.x)
+        self.grad_x = torch.empty_like(self.x)
+        self.grad_f = torch.empty_like(self.f)
+        self.grad_R = torch.empty(T, m, n, device=device)
+        self.grad_H = torch.empty(T, n, n, device=device)
+        self.grad_W = torch.empty(T, n, m, device=device)
+        self.grad_v = torch.empty(T, n, device=device) if proj else None
+        self.code = _lib.dtype_code(torch.bfloat16)
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        self._ptr = _lib.ptr
+
+    def read_fwd(self):
+        self._check(self.lib.hc_read_fwd(self.R.data_ptr(), self.x.data_ptr(), self.u.data_ptr(), self.T, self.n,
+                                         self.m, self.D, self.code, self.stream), "hc_read_fwd")
+
+    def read_bwd(self):
+        self._check(self.lib.hc_read_bwd(self.g_u.data_ptr(), self.R.data_ptr(), self.x.data_ptr(),
+                                         self.grad_x.data_ptr(), self.grad_R.data_ptr(), self.T, self.n, self.m,
+                                         self.D, self.code, self.stream), "hc_read_bwd")
+
+    def mix_write_fwd(self):
+        self._check(self.lib.hc_mix_write_fwd(self.H.data_ptr(), self.x.data_ptr(), self.W.data_ptr(),
+                                              self.f.data_ptr(), self._ptr(self.v), self.out.data_ptr(), self.T,
+                                              self.n, self.m, self.D, self.code, self.stream), "hc_mix_write_fwd")
+
+    def mix_write_bwd(self):
+        self._check(self.lib.hc_mix_write_bwd(self.g_x.data_ptr(), self.H.data_ptr(), self.x.data_ptr(),
+                                              self.W.data_ptr(), self.f.data_ptr(), self._ptr(self.v),
+                                              self.grad_x.data_ptr(), self.grad_f.data_ptr(),
+                                              self.grad_H.data_ptr(), self.grad_W.data_ptr(),
+                                              self._ptr(self.grad_v), self.T, self.n, self.m, self.D, self.code,
+                                              self.stream), "hc_mix_write_bwd")
+
+
+def time_launches(device, fns, steps, warmup):
+    """Mean device ms of each callable in `fns`, L2 flushed between steps."""
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    for _ in range(warmup):
+        for fn in fns:
+            fn()
+    torch.cuda.synchronize(device)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)] for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(float(i))
+        evs[i][0].record()
+        for k, fn in enumerate(fns):
+            fn()
+            evs[i][k + 1].record()
+    torch.cuda.synchronize(device)
+    del flush
+    return [float(np.mean([e[k].elapsed_time(e[k + 1]) for e in evs])) for k in range(len(fns))]
+
+
+# (n, m, D, projection) of the two-phase sweep; the first is the fused step's shape
+RW_SWEEP = ((4, 1, 768, False), (4, 1, 768, True), (4, 2, 768, False), (4, 4, 512, False), (6, 3, 1024, True),
+            (2, 1, 2048, False), (8, 4, 1024, False))
+
+SWEEP_N = (2, 3, 4, 6, 8)
+SWEEP_D = (512, 1024, 2048, 4096)
+
+
+def run_sweep(args):
+    """The small-n sweep at 16,384 tokens, bf16: one JSON line per (n, D) with
+    the fused fwd+bwd GB/s and its fraction of the HBM peak; one line per
+    (n, m, D, projection) for the two-phase read / mix-write kernels; then one
+    line per n for the per-token batched expm (16,384 matrices, fwd+bwd)."""
+    _, _, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from hyperconnections_b200 import _lib
+
+    _lib.lib()
+    peak, peak_kind = measured_peak()
+    steps = max(5, min(args.steps, 50))
+    for n in SWEEP_N:
+        for D in SWEEP_D:
+            res = time_fused(device, steps, args.warmup, 1, T=TOKENS, n=n, D=D)
+            fwd_ms, bwd_ms = float(np.mean(res["fwd_ms"])), float(np.mean(res["bwd_ms"]))
+            fb, bb = fused_bytes(TOKENS, n, D)
+            gbs = (fb + bb) / ((fwd_ms + bwd_ms) * 1e-3) / 1e9
+            print(json.dumps({
+                "sweep": "fused", "tokens": TOKENS, "n": n, "D": D, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                "fwd_gbs": fb / (fwd_ms * 1e-3) / 1e9, "bwd_gbs": bb / (bwd_ms * 1e-3) / 1e9, "gbs": gbs,
+                "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": peak_kind,
+                "pct_of_8tbs": 100.0 * gbs / NOMINAL_HBM_GBS, "bytes": fb + bb}), flush=True)
+    for n, m, D, proj in RW_SWEEP:
+        r = RwRunner(device, TOKENS, n, m, D, proj)
+        names = ("read_fwd", "read_bwd", "mix_write_fwd", "mix_write_bwd")
+        ms = time_launches(device, [getattr(r, k) for k in names], steps, args.warmup)
+        nbytes = rw_bytes(TOKENS, n, m, D, proj)
+        line = {"sweep": "read/mix_write", "tokens": TOKENS, "n": n, "m": m, "D": D, "proj": proj,
+                "peak": peak, "peak_kind": peak_kind}
+        for k, t in zip(names, ms):
+            line[f"{k}_ms"] = t
+            line[f"{k}_gbs"] = nbytes[k] / (t * 1e-3) / 1e9
+        line["gbs"] = sum(nbytes.values()) / (sum(ms) * 1e-3) / 1e9
+        line["frac_of_peak"] = line["gbs"] / peak
+        print(json.dumps(line), flush=True)
+        del r
+    for n in SWEEP_N:
+        ms = float(np.mean(time_expm(device, steps, args.warmup, B=TOKENS, n=n)))
+        print(json.dumps({"sweep": "expm_t18", "batch": TOKENS, "n": n, "ms_per_step": ms,
+                          "matrices_per_s": TOKENS / (ms * 1e-3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -517,10 +719,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sweep", action="store_true", help="print the n x D sweep (16,384 tokens) instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

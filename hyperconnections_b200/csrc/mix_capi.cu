@@ -4,7 +4,7 @@
 // dtype codes, NULL pointers and alignment. The 16-byte vector path is taken
 // when D is a multiple of the chunk width and every stream base pointer is
 // 16-byte aligned; otherwise the element-wise path of the same kernels runs.
-#include "mix_warp.cuh"
+#include "rw_warp.cuh"
 
 namespace hc {
 namespace {
@@ -48,17 +48,6 @@ int run_bwd(int sdt, bool fused, bool proj, bool vec, bool pf32, int n, const Mi
 }
 
 bool params_aligned(int pdt, const void* p) { return pdt != HC_DTYPE_F32 || p == nullptr || aligned4(p); }
-
-int sm_count() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
-  if (dev < 64 && cached[dev] > 0) return cached[dev];
-  int n = 0;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  if (dev < 64) cached[dev] = n;
-  return n;
-}
 
 int run_fwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const WarpGeometry& g, const MixFwdArgs& a,
                 cudaStream_t s) {
@@ -197,8 +186,10 @@ extern "C" int hc_fused_bwd(const void* g_u, const void* g_x, const void* x, con
 extern "C" int hc_wait_timeouts(unsigned int* count, int reset) {
   if (!count) return HC_ERR_NULL_POINTER;
   if (cudaDeviceSynchronize() != cudaSuccess) return HC_ERR_LAUNCH;
-  *count = mix_warp_take_timeouts_f32(reset != 0) + mix_warp_take_timeouts_f16(reset != 0) +
-           mix_warp_take_timeouts_bf16(reset != 0);
+  const bool r = reset != 0;
+  *count = mix_warp_take_timeouts_f32(r) + mix_warp_take_timeouts_f16(r) + mix_warp_take_timeouts_bf16(r) +
+           rw_fwd_take_timeouts_f32(r) + rw_fwd_take_timeouts_f16(r) + rw_fwd_take_timeouts_bf16(r) +
+           rw_bwd_take_timeouts_f32(r) + rw_bwd_take_timeouts_f16(r) + rw_bwd_take_timeouts_bf16(r);
   return HC_OK;
 }
 

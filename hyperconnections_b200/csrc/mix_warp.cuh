@@ -2,7 +2,7 @@
 //
 // A persistent CTA per SM owns a contiguous range of tokens and a ring of
 // shared-memory stages, each with a "full" and an "empty" mbarrier. Warp 0 is
-// the producer: one lane issues the bulk copies (cp.async.bulk, no multicast)
+// the producer: one lane issues the bulk copies (plain cp.async.bulk into this CTA only)
 // of the next token (or token-slice) into the next free stage with
 // arrive.expect_tx on its full barrier. Warps 1..C are consumers: consumer c
 // takes tokens c, c + C, ... of the range, waits on the stage's full barrier,
@@ -68,7 +68,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// 1-D bulk copy global -> this CTA's shared memory (no multicast).
+// 1-D bulk copy global -> this CTA's shared memory (one destination CTA).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -1016,11 +1016,10 @@ WarpTuning& warp_tuning();
 //     per row slice);
 //   * tokens smaller than the item target are grouped, tpi per item, so that
 //     one bulk copy per tensor moves several tokens.
-inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
+inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
                           int num_sms) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
   const WarpTuning tune = warp_tuning();
-  const int rows = warp_rows(bwd, fused, n);
   const int budget = 200 * 1024;
   const int64_t max_stage = 24 * 1024;
   const int64_t item_target = tune.stage_bytes > 0 ? tune.stage_bytes : 12 * 1024;
@@ -1040,7 +1039,7 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_
   geo.stage_bytes = static_cast<int>(tpi * rows * sl * esize);
   int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
   if (tune.stages > 0) stages = std::min(stages, tune.stages);
-  int consumers = std::min(warp_cap(bwd, n) - 1, stages - 2);
+  int consumers = std::min(warp_cap_ - 1, stages - 2);
   if (tune.warps > 0) consumers = std::min(consumers, tune.warps);
   if (consumers < 1 || stages < 3) return false;
   geo.stages = stages;
@@ -1048,6 +1047,11 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_
   geo.smem_bytes = stages * geo.stage_bytes;
   geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
   return true;
+}
+
+inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
+                          int num_sms) {
+  return ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms);
 }
 
 template <typename KernelT>

@@ -1,0 +1,117 @@
+// rw_capi.cu — C entry points of the width-read and mix + depth-write kernels
+// for a general backbone width m (see hcops.h).
+//
+// Host-side checks come first (sizes, dtype, NULL pointers, alignment). The
+// ring kernels run when 1 <= m <= min(n, 4), D is a multiple of 16 bytes of
+// elements and every stream base is 16-byte aligned; any other shape runs
+// the element-wise kernels of the same arithmetic.
+#include "rw_warp.cuh"
+
+namespace hc {
+namespace {
+
+constexpr int64_t kMaxD = int64_t(1) << 24;
+constexpr int64_t kMaxTokens = (int64_t(1) << 31) - 1;
+
+int check_rw(int64_t T, int n, int m, int64_t D, int sdt) {
+  if (T < 0 || T > kMaxTokens || D < 0 || D > kMaxD) return HC_ERR_BAD_SIZE;
+  if (n < 1 || n > 8 || m < 1 || m > 4) return HC_ERR_UNSUPPORTED_N;
+  if (dtype_size(sdt) == 0) return HC_ERR_DTYPE;
+  return HC_OK;
+}
+
+bool f32_aligned(const float* p) { return p == nullptr || aligned4(p); }
+
+bool stream_ok(const void* p) { return p == nullptr || aligned16(p); }
+
+int dispatch(bool bwd, int sdt, bool ring, bool mixw, bool proj, int n, int m, const WarpGeometry& g,
+             const RwArgs& a, cudaStream_t s) {
+  switch (sdt) {
+    case HC_DTYPE_F32: return bwd ? rw_bwd_f32(ring, mixw, proj, n, m, g, a, s) : rw_fwd_f32(ring, mixw, proj, n, m, g, a, s);
+    case HC_DTYPE_F16: return bwd ? rw_bwd_f16(ring, mixw, proj, n, m, g, a, s) : rw_fwd_f16(ring, mixw, proj, n, m, g, a, s);
+    case HC_DTYPE_BF16: return bwd ? rw_bwd_bf16(ring, mixw, proj, n, m, g, a, s) : rw_fwd_bf16(ring, mixw, proj, n, m, g, a, s);
+  }
+  return HC_ERR_DTYPE;
+}
+
+// Ring geometry when the shape and the pointers allow it.
+bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, int64_t T, int64_t D, int sdt,
+             bool streams_aligned) {
+  const int es = dtype_size(sdt);
+  if (!streams_aligned || !rw_ring_supported(n, m) || D % (16 / es) != 0) return false;
+  return ring_geometry(geo, rw_rows(bwd, n, m, mixw), rw_cap(bwd, n, m, mixw, proj), T, D, es, sm_count());
+}
+
+}  // namespace
+}  // namespace hc
+
+using namespace hc;
+
+extern "C" int hc_read_fwd(const float* R, const void* x, void* u, int64_t T, int n, int m, int64_t D,
+                           int stream_dtype, void* stream) {
+  int rc = check_rw(T, n, m, D, stream_dtype);
+  if (rc) return rc;
+  if (T == 0 || D == 0) return HC_OK;
+  if (!R || !x || !u) return HC_ERR_NULL_POINTER;
+  if (!f32_aligned(R)) return HC_ERR_ALIGNMENT;
+  RwArgs a{};
+  a.x = x; a.R = R; a.out = u; a.T = T; a.D = D;
+  WarpGeometry geo{};
+  const bool ring = ring_ok(geo, false, false, false, n, m, T, D, stream_dtype, aligned16(x) && aligned16(u));
+  return dispatch(false, stream_dtype, ring, false, false, n, m, geo, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hc_read_bwd(const void* g_u, const float* R, const void* x, void* grad_x, float* grad_R, int64_t T,
+                           int n, int m, int64_t D, int stream_dtype, void* stream) {
+  int rc = check_rw(T, n, m, D, stream_dtype);
+  if (rc) return rc;
+  if (T == 0) return HC_OK;
+  if (!R) return HC_ERR_NULL_POINTER;
+  if (D > 0 && (!g_u || !x)) return HC_ERR_NULL_POINTER;
+  if (!f32_aligned(R) || !f32_aligned(grad_R)) return HC_ERR_ALIGNMENT;
+  RwArgs a{};
+  a.g = g_u; a.x = x; a.R = R; a.grad_x = D > 0 ? grad_x : nullptr; a.grad_R = grad_R; a.T = T; a.D = D;
+  WarpGeometry geo{};
+  const bool ring = ring_ok(geo, true, false, false, n, m, T, D, stream_dtype,
+                            aligned16(g_u) && aligned16(x) && stream_ok(grad_x));
+  // D == 0 still writes the (all-zero) grad_R through the element-wise kernel.
+  return dispatch(true, stream_dtype, ring, false, false, n, m, geo, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hc_mix_write_fwd(const float* H, const void* x, const float* W, const void* f, const float* v,
+                                void* out, int64_t T, int n, int m, int64_t D, int stream_dtype, void* stream) {
+  int rc = check_rw(T, n, m, D, stream_dtype);
+  if (rc) return rc;
+  if (T == 0 || D == 0) return HC_OK;
+  if (!H || !x || !W || !f || !out) return HC_ERR_NULL_POINTER;
+  if (!f32_aligned(H) || !f32_aligned(W) || !f32_aligned(v)) return HC_ERR_ALIGNMENT;
+  RwArgs a{};
+  a.x = x; a.f = f; a.H = H; a.W = W; a.v = v; a.out = out; a.T = T; a.D = D;
+  const bool proj = v != nullptr;
+  WarpGeometry geo{};
+  const bool ring = ring_ok(geo, false, true, proj, n, m, T, D, stream_dtype,
+                            aligned16(x) && aligned16(f) && aligned16(out));
+  return dispatch(false, stream_dtype, ring, true, proj, n, m, geo, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hc_mix_write_bwd(const void* g, const float* H, const void* x, const float* W, const void* f,
+                                const float* v, void* grad_x, void* grad_f, float* grad_H, float* grad_W,
+                                float* grad_v, int64_t T, int n, int m, int64_t D, int stream_dtype, void* stream) {
+  int rc = check_rw(T, n, m, D, stream_dtype);
+  if (rc) return rc;
+  if (T == 0) return HC_OK;
+  if (!H || !W) return HC_ERR_NULL_POINTER;
+  if (D > 0 && (!g || !x || !f)) return HC_ERR_NULL_POINTER;
+  if (!f32_aligned(H) || !f32_aligned(W) || !f32_aligned(v) || !f32_aligned(grad_H) || !f32_aligned(grad_W) ||
+      !f32_aligned(grad_v))
+    return HC_ERR_ALIGNMENT;
+  RwArgs a{};
+  a.g = g; a.x = x; a.f = f; a.H = H; a.W = W; a.v = v;
+  a.grad_x = D > 0 ? grad_x : nullptr; a.grad_f = D > 0 ? grad_f : nullptr;
+  a.grad_H = grad_H; a.grad_W = grad_W; a.grad_v = v ? grad_v : nullptr; a.T = T; a.D = D;
+  const bool proj = v != nullptr;
+  WarpGeometry geo{};
+  const bool ring = ring_ok(geo, true, true, proj, n, m, T, D, stream_dtype,
+                            aligned16(g) && aligned16(x) && aligned16(f) && stream_ok(grad_x) && stream_ok(grad_f));
+  return dispatch(true, stream_dtype, ring, true, proj, n, m, geo, a, static_cast<cudaStream_t>(stream));
+}

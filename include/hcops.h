@@ -18,6 +18,7 @@
  *   projection direction v                  [T, n]      param dtype
  *   read weights alpha, write weights beta  [T, n]      float32
  *   matrices for expm A, E, G, dA           [batch, n, n] float32
+ *   m-block read / write: R [T,m,n], W [T,n,m] float32; f, u [T,m,D] stream dtype
  * All gradients of per-token parameters are written as float32.
  *
  * Citations name the reference interface each entry point replaces
@@ -36,7 +37,7 @@ extern "C" {
 #define HC_OK                 0
 #define HC_ERR_NULL_POINTER   1  /* a required pointer is NULL                     */
 #define HC_ERR_BAD_SIZE       2  /* negative size, or n / D out of range           */
-#define HC_ERR_UNSUPPORTED_N  3  /* n outside 1..8                                 */
+#define HC_ERR_UNSUPPORTED_N  3  /* n outside 1..8 (or m outside 1..4)            */
 #define HC_ERR_DTYPE          4  /* unknown dtype code or unsupported combination  */
 #define HC_ERR_ALIGNMENT      5  /* a float32 pointer is not 4-byte aligned        */
 #define HC_ERR_SCRATCH        6  /* scratch buffer missing or too small            */
@@ -50,7 +51,8 @@ extern "C" {
 /* Text for a status code (static storage). */
 const char* hc_error_string(int code);
 
-/* Library ABI version; bumped whenever a signature below changes. */
+/* Library ABI version; bumped whenever a signature below changes or an entry
+ * point is added. */
 int hc_abi_version(void);
 
 /* Diagnostics: synchronises the current device, then stores in *count how
@@ -182,6 +184,52 @@ int hc_fused_bwd(const void* g_u, const void* g_x, const void* x,
                  const float* beta, void* grad_x, void* grad_f,
                  float* grad_H, float* grad_alpha, float* grad_beta,
                  int64_t T, int n, int64_t D, int stream_dtype, void* stream);
+
+/* ===========================================================================
+ * Width-read and mix + depth-write for a backbone of m blocks
+ * (1 <= m <= 4, 1 <= n <= 8): the two halves of a hyper-connection layer,
+ * one before and one after the wrapped module. Weights are float32, streams
+ * share stream_dtype, every output is written whole.
+ * ======================================================================== */
+
+/* u[t,k,:] = sum_j R[t,k,j] x[t,j,:]      R [T,m,n], x [T,n,D] -> u [T,m,D]
+ * Replaces: hyperconnections/cghc.py:410 einsum(read_in, x,
+ * "b m n, b n d -> b m d"), and the same read at ghc.py:116, mhc.py:138,
+ * attnhc.py:154. */
+int hc_read_fwd(const float* R, const void* x, void* u, int64_t T, int n,
+                int m, int64_t D, int stream_dtype, void* stream);
+
+/* Given g_u = dL/du [T,m,D]:
+ *   grad_x[t,j,:] = sum_k R[t,k,j] g_u[t,k,:]   [T,n,D] stream dtype (nullable)
+ *   grad_R[t,k,j] = sum_d g_u[t,k,d] x[t,j,d]   [T,m,n] float32      (nullable)
+ * Replaces the autograd backward of the read einsum (cghc.py:410). */
+int hc_read_bwd(const void* g_u, const float* R, const void* x, void* grad_x,
+                float* grad_R, int64_t T, int n, int m, int64_t D,
+                int stream_dtype, void* stream);
+
+/* out[t,i,:] = sum_j H_ij x_j [+ (v_i - (H v)_i) (v^T x)] + sum_k W_ik f_k
+ * H [T,n,n], W [T,n,m], v [T,n] or NULL, x [T,n,D], f [T,m,D] -> out [T,n,D].
+ * Replaces: cghc.py:417 einsum(write_out, out, "b n m, b m d -> b n d")
+ * followed by :449 stream_mix_add (ops/stream_mix.py:57), without
+ * materialising the written term Y. */
+int hc_mix_write_fwd(const float* H, const void* x, const float* W,
+                     const void* f, const float* v, void* out, int64_t T,
+                     int n, int m, int64_t D, int stream_dtype, void* stream);
+
+/* Given g = dL/dout [T,n,D]; with v: s = v^T x, c = v - H v, b = c^T g:
+ *   grad_x_j  = sum_i H_ij g_i [+ v_j b]            [T,n,D] (nullable)
+ *   grad_f_k  = sum_i W_ik g_i                      [T,m,D] (nullable)
+ *   grad_H_ij = sum_d g_i (x_j [- v_j s])           [T,n,n] float32 (nullable)
+ *   grad_W_ik = sum_d g_i f_k                       [T,n,m] float32 (nullable)
+ *   grad_v    = rho - H^T rho + sum_d b x, rho_i = sum_d g_i s
+ *                                                   [T,n]   float32 (nullable)
+ * Replaces the autograd backward of the write einsum (cghc.py:417) and
+ * stream_mix_small_nb.py:341-391. */
+int hc_mix_write_bwd(const void* g, const float* H, const void* x,
+                     const float* W, const void* f, const float* v,
+                     void* grad_x, void* grad_f, float* grad_H, float* grad_W,
+                     float* grad_v, int64_t T, int n, int m, int64_t D,
+                     int stream_dtype, void* stream);
 
 #ifdef __cplusplus
 }

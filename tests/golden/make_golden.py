@@ -13,7 +13,9 @@ What runs, all from the reference checkout, unmodified:
     (the autotuner needs a GPU) -> stream_mix_*.npz;
   * CGHC's composition read einsum (cghc.py:410) -> write einsum (:417) ->
     stream_mix_add (:449, the small-NB Function) in float32 on bf16-exact
-    inputs, forward and backward -> fused.npz.
+    inputs, forward and backward -> fused.npz;
+  * the same composition for m backbone blocks with the reference's own
+    einops patterns, with and without the projection direction -> rw.npz.
 
 The reference imports timm only for trunc_normal_; a stub providing
 torch.nn.init.trunc_normal_ is written to a temporary directory and put on
@@ -219,6 +221,52 @@ def gen_fused(ref_small, out):
     np.savez_compressed(os.path.join(out, "fused.npz"), **rec)
 
 
+def gen_rw(ref_small, out):
+    """Read einsum (cghc.py:410) and write einsum (:417) with the reference's
+    own einops patterns, then the mix through stream_mix_add (:449), for
+    general m, with and without the projection direction; float32 math on
+    bf16-exact inputs. Shapes include the reference test CONFIGS
+    (tests/test_cghc.py:21-26, test_ghc.py:22-29: (n, m, embed_dim) with
+    block size embed_dim / m) and 16-byte-aligned block sizes."""
+    from einops import einsum
+
+    fn = ref_small.stream_mix_add_small_nb
+    cases = [  # (T, n, m, D, proj)
+        (6, 2, 1, 8, False), (6, 4, 2, 4, False), (5, 4, 4, 2, True), (4, 6, 3, 4, False), (6, 2, 2, 4, True),
+        (16, 4, 2, 64, True), (8, 8, 4, 128, False), (12, 3, 3, 40, True), (10, 6, 2, 48, False),
+        (6, 2, 2, 100, True), (20, 4, 1, 96, True), (9, 8, 1, 64, True), (7, 5, 4, 72, True),
+    ]
+    rec = {}
+    for ci, (T, n, m, D, proj) in enumerate(cases):
+        g = torch.Generator().manual_seed(3000 + ci)
+        bf = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).float()  # noqa: E731
+        x = bf(T, n, D)
+        f = bf(T, m, D)
+        R = torch.sigmoid(torch.randn(T, m, n, generator=g))          # read_in  [B, m, n]
+        W = 2 * torch.sigmoid(torch.randn(T, n, m, generator=g))      # write_out [B, n, m]
+        S = torch.triu(0.5 * torch.randn(T, n, n, generator=g), 1)
+        H = torch.linalg.matrix_exp(S - S.mT)
+        v = torch.nn.functional.normalize(torch.randn(T, n, generator=g), dim=-1) if proj else None
+        g_u = bf(T, m, D)
+        g_x = bf(T, n, D)
+        X, Fv, Rr, Wr, Hr = (t.clone().requires_grad_(True) for t in (x, f, R, W, H))
+        Vr = v.clone().requires_grad_(True) if proj else None
+        u = einsum(Rr, X, "b m n, b n d -> b m d")                     # cghc.py:410
+        Y = einsum(Wr, Fv, "b n m, b m d -> b n d")                    # cghc.py:417
+        x_out = fn(Hr, X, Y, Vr)                                       # cghc.py:449 -> :363
+        torch.autograd.backward([u, x_out], [g_u, g_x])
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([T, n, m, D, int(proj)])
+        items = [("x", x), ("f", f), ("R", R), ("W", W), ("H", H), ("g_u", g_u), ("g_x", g_x),
+                 ("u", u.detach()), ("x_out", x_out.detach()), ("grad_x", X.grad), ("grad_f", Fv.grad),
+                 ("grad_R", Rr.grad), ("grad_W", Wr.grad), ("grad_H", Hr.grad)]
+        if proj:
+            items += [("v", v), ("grad_v", Vr.grad)]
+        for name, t in items:
+            rec[f"{key}_{name}"] = t.numpy()
+    np.savez_compressed(os.path.join(out, "rw.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -228,6 +276,7 @@ def main():
     gen_expm(ref_expm, args.out)
     gen_stream_mix(ref_small, args.out)
     gen_fused(ref_small, args.out)
+    gen_rw(ref_small, args.out)
     for name in sorted(os.listdir(args.out)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")

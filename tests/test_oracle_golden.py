@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 from oracle import expm as oexpm
+from oracle import rw as orw
 from oracle import stream_mix as omix
 from tests.conftest import load_golden
 
@@ -12,6 +13,7 @@ EXPM = load_golden("expm.npz")
 MIX32 = load_golden("stream_mix_f32.npz")
 MIX16 = load_golden("stream_mix_f16.npz")
 FUSED = load_golden("fused.npz")
+RW = load_golden("rw.npz")
 
 EXPM_KEYS = sorted({k.rsplit("_", 1)[0] for k in EXPM if k.endswith("_A")})
 
@@ -88,3 +90,22 @@ def test_oracle_fused_matches_reference_composition(case):
     grads = omix.fused_bwd(g("g_u"), g("g_x"), g("x"), g("f"), g("H"), g("alpha"), g("beta"))
     for name, got in zip(("grad_x", "grad_f", "grad_H", "grad_alpha", "grad_beta"), grads):
         np.testing.assert_allclose(got, g(name), rtol=1e-4, atol=1e-4, err_msg=name)
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in RW}))
+def test_oracle_read_mix_write_matches_reference(case):
+    """m-block read (einsum, cghc.py:410) and write + mix (:417, :449), with
+    and without the projection direction."""
+    g = lambda name: RW[f"{case}_{name}"]  # noqa: E731
+    proj = bool(g("meta")[4])
+    v = g("v") if proj else None
+    np.testing.assert_allclose(orw.read_fwd(g("R"), g("x")), g("u"), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(orw.mix_write_fwd(g("H"), g("x"), g("W"), g("f"), v), g("x_out"),
+                               rtol=1e-5, atol=1e-5)
+    gR, gx_read = orw.read_bwd(g("g_u"), g("R"), g("x"))
+    gH, gx_mix, gW, gf, gv = orw.mix_write_bwd(g("g_x"), g("H"), g("x"), g("W"), g("f"), v)
+    np.testing.assert_allclose(gx_read + gx_mix, g("grad_x"), rtol=1e-4, atol=1e-4)
+    for name, got in (("grad_R", gR), ("grad_W", gW), ("grad_f", gf), ("grad_H", gH)):
+        np.testing.assert_allclose(got, g(name), rtol=1e-4, atol=1e-4, err_msg=name)
+    if proj:
+        np.testing.assert_allclose(gv, g("grad_v"), rtol=1e-4, atol=1e-4)
