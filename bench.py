@@ -18,8 +18,9 @@ is reported alongside in matrices/s.
 
 Timing: CUDA events on the launching stream around each kernel, L2 flushed
 (a 256 MiB write) between steps outside the events, barrier + synchronize
-around the K timed steps, max over ranks. Under torchrun every rank runs the
-full workload on its own GPU with no collective on the data path (weak
+around the K timed steps, max over ranks. Under torchrun every rank runs one
+full batch of the workload on its own GPU (its shard of an N x 16,384-token
+global batch, seeded by rank) with no collective on the data path (weak
 scaling); value = N * bytes / max-rank time.
 
 ``--impl reference`` times the reference's own CPU path for the same work
@@ -191,6 +192,16 @@ def max_over_ranks(value: float, world: int, device) -> float:
     return float(t.item())
 
 
+def gather_ranks(value: float, world: int, device) -> list:
+    """Every rank's value, in rank order (one all-gather; [value] at N = 1)."""
+    if world == 1:
+        return [value]
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def barrier(world: int):
     if world > 1:
         torch.distributed.barrier()
@@ -236,8 +247,8 @@ class FusedRunner:
         self._check(rc, "hc_fused_bwd")
 
 
-def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK):
-    runner = FusedRunner(device, T=T, n=n, D=D)
+def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0):
+    runner = FusedRunner(device, T=T, n=n, D=D, seed=seed)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for _ in range(warmup):
@@ -496,7 +507,8 @@ def run_b200(args):
 
     sampler = ClockSampler(local)
     sampler.start()
-    res = time_fused(device, args.steps, args.warmup, world)
+    # rank r's shard: its own seeded batch of the workload (seed r)
+    res = time_fused(device, args.steps, args.warmup, world, seed=dist_env()[1])
     t0, t1 = res["wall"]
     clocks = sampler.window(t0, t1)
 
@@ -504,6 +516,7 @@ def run_b200(args):
     bwd_ms = float(np.mean(res["bwd_ms"]))
     step_ms = fwd_ms + bwd_ms
     step_ms_max = max_over_ranks(step_ms, world, device)
+    rank_ms = gather_ranks(step_ms, world, device)
     fb, bb = fused_bytes(TOKENS, N_STREAMS, BLOCK)
     value = world * (fb + bb) / (step_ms_max * 1e-3) / 1e9
 
@@ -539,6 +552,7 @@ def run_b200(args):
             "pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
             "pct_of_measured_hbm": 100.0 * value / world / peak,
             "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms},
+            "rank_ms_per_step": rank_ms,
             "roofline": {
                 "bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,

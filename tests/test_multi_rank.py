@@ -35,8 +35,9 @@ def _worker(rank, world, port, q):
 
         # Each rank's step time differs; every rank must see the slowest.
         slowest = bench.max_over_ranks(1.5 + rank, world, torch.device("cpu"))
+        every = bench.gather_ranks(1.5 + rank, world, torch.device("cpu"))
         bench.barrier(world)
-        q.put((rank, slowest, bench.dist_env()))
+        q.put((rank, slowest, every, bench.dist_env()))
     finally:
         dist.destroy_process_group()
 
@@ -53,8 +54,9 @@ def test_max_over_ranks_gloo():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, slowest, env in got:
+    for rank, slowest, every, env in got:
         assert slowest == 1.5 + (world - 1)
+        assert every == [1.5 + r for r in range(world)]
         assert env == (world, rank, rank)
 
 
