@@ -15,7 +15,11 @@ What runs, all from the reference checkout, unmodified:
     stream_mix_add (:449, the small-NB Function) in float32 on bf16-exact
     inputs, forward and backward -> fused.npz;
   * the same composition for m backbone blocks with the reference's own
-    einops patterns, with and without the projection direction -> rw.npz.
+    einops patterns, with and without the projection direction -> rw.npz;
+  * one CGHC layer (cghc.py) per generator type and projection mode: its own
+    read/write weights, generator, projection and forward output, with the
+    gradients of its read -> module -> write -> matrix_exp -> mix chain
+    -> layer.npz.
 
 The reference imports timm only for trunc_normal_; a stub providing
 torch.nn.init.trunc_normal_ is written to a temporary directory and put on
@@ -267,6 +271,70 @@ def gen_rw(ref_small, out):
     np.savez_compressed(os.path.join(out, "rw.npz"), **rec)
 
 
+def gen_layer(ref_path, out):
+    """One CGHC layer of the reference (hyperconnections/cghc.py), eager path,
+    float32: its own read/write weights (:323-339), generator (:219-315) and
+    projection (:341-350) for a seeded input, the layer's own forward output,
+    and the gradients of the chain read (:410) -> module -> write (:417) ->
+    matrix_exp (:321) -> mix (:449) with respect to x, the weights, the
+    generator, the projection direction and the wrapped Linear's parameters.
+    The chain is checked against the layer's forward before it is saved."""
+    from einops import einsum
+    from hyperconnections.cghc import ContinuousGenHyperConnections as CGHC
+
+    configs = [  # (n, m, embed_dim, generator_type, projection, vec_dt)
+        (4, 1, 64, "conservative_psd_diss", "none", False),
+        (4, 2, 128, "conservative_diag_diss", "mean", False),
+        (6, 3, 96, "conservative_laplacian", "v", True),
+        (2, 1, 8, "conservative", "none", False),
+        (4, 4, 8, "psd_diss", "v", False),
+        (8, 2, 128, "laplacian", "mean", True),
+    ]
+    rec = {}
+    for ci, (n, m, E, gen, proj, vec_dt) in enumerate(configs):
+        torch.manual_seed(4000 + ci)
+        block = E // m
+        inp = n * block
+        module = torch.nn.Linear(E, E)
+        layer = CGHC(n, m, inp, E, module, dt=0.3, generator_type=gen, projection=proj, vec_dt=vec_dt,
+                     use_triton=False)
+        with torch.no_grad():  # move the static parameters off their init values
+            for name, prm in layer.named_parameters():
+                if not name.startswith("module.") and prm.dim() >= 1:
+                    prm.add_(0.3 * torch.randn_like(prm))
+        B, S = 2, 5
+        x = torch.randn(B, S, inp).to(torch.bfloat16).float()
+        g = torch.randn(B, S, inp)
+        with torch.no_grad():
+            ref_out = layer(x)
+        xf = x.reshape(-1, n, block)
+        with torch.no_grad():
+            write_out, read_in = layer.compute_read_write_weights(xf)
+            A = layer.compute_generator(xf)
+            v = layer.compute_projection(xf)
+        X, RI, WO, AL = (t.detach().clone().requires_grad_(True) for t in (xf, read_in, write_out, A))
+        V = None if v is None else v.detach().clone().requires_grad_(True)
+        u = einsum(RI, X, "b m n, b n d -> b m d")                              # cghc.py:410
+        f = layer.module(u.reshape(B, S, E)).reshape(-1, m, block)
+        Y = einsum(WO, f, "b n m, b m d -> b n d")                             # cghc.py:417
+        Phi = torch.linalg.matrix_exp(AL.float()).to(x.dtype)                  # cghc.py:321
+        outc = layer._stream_mix(X, Phi, Y, V)                                   # cghc.py:449
+        assert torch.allclose(outc.reshape(B, S, inp), ref_out, rtol=1e-6, atol=1e-6)
+        layer.zero_grad()
+        outc.backward(g.reshape(-1, n, block))
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([n, m, E, block, B * S, int(V is not None)])
+        items = [("x", xf), ("read_in", read_in), ("write_out", write_out), ("A", A), ("g", g.reshape(-1, n, block)),
+                 ("W_mod", module.weight.detach()), ("b_mod", module.bias.detach()), ("out", ref_out.reshape(-1, n, block)),
+                 ("grad_x", X.grad), ("grad_read_in", RI.grad), ("grad_write_out", WO.grad), ("grad_A", AL.grad),
+                 ("grad_W_mod", module.weight.grad), ("grad_b_mod", module.bias.grad)]
+        if V is not None:
+            items += [("v", v), ("grad_v", V.grad)]
+        for name, t in items:
+            rec[f"{key}_{name}"] = t.detach().numpy()
+    np.savez_compressed(os.path.join(out, "layer.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -277,6 +345,7 @@ def main():
     gen_stream_mix(ref_small, args.out)
     gen_fused(ref_small, args.out)
     gen_rw(ref_small, args.out)
+    gen_layer(args.reference, args.out)
     for name in sorted(os.listdir(args.out)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")

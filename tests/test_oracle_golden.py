@@ -109,3 +109,47 @@ def test_oracle_read_mix_write_matches_reference(case):
         np.testing.assert_allclose(got, g(name), rtol=1e-4, atol=1e-4, err_msg=name)
     if proj:
         np.testing.assert_allclose(gv, g("grad_v"), rtol=1e-4, atol=1e-4)
+
+
+LAYER = load_golden("layer.npz")
+LAYER_CASES = sorted({k.split("_")[0] for k in LAYER})
+
+
+def layer_chain_oracle(g):
+    """Float64 oracle of one CGHC layer's chain: read -> Linear -> write ->
+    matrix_exp -> mix, forward and backward (cghc.py:321, :410, :417, :449)."""
+    x, R, W, A, G = g("x"), g("read_in"), g("write_out"), g("A"), g("g")
+    Wm, bm = g("W_mod").astype(np.float64), g("b_mod").astype(np.float64)
+    T, n, block = x.shape
+    m = R.shape[1]
+    v = g("v") if bool(g("meta")[5]) else None
+    vt = None if v is None else np.broadcast_to(v, (T, n))
+    Phi = np.stack([oexpm.expm_pade(a[None])[0] for a in A.astype(np.float64)])
+    u = orw.read_fwd(R, x)
+    f = (u.reshape(T, m * block) @ Wm.T + bm).reshape(T, m, block)
+    out = orw.mix_write_fwd(Phi, x, W, f, vt)
+    gPhi, gx_mix, gW, gf, gv = orw.mix_write_bwd(G, Phi, x, W, f, vt)
+    gf_flat = gf.reshape(T, m * block)
+    grads = {
+        "grad_W_mod": gf_flat.T @ u.reshape(T, m * block),
+        "grad_b_mod": gf_flat.sum(0),
+        "grad_write_out": gW,
+        "grad_A": oexpm.expm_pade_grad(A.astype(np.float64), gPhi),
+    }
+    gR, gx_read = orw.read_bwd((gf_flat @ Wm).reshape(T, m, block), R, x)
+    grads["grad_read_in"] = gR
+    grads["grad_x"] = gx_mix + gx_read
+    if v is not None:
+        grads["grad_v"] = gv.sum(0, keepdims=True) if v.shape[0] == 1 else gv
+    return out, grads
+
+
+@pytest.mark.parametrize("case", LAYER_CASES)
+def test_oracle_cghc_layer_chain_matches_reference(case):
+    g = lambda name: LAYER[f"{case}_{name}"]  # noqa: E731
+    out, grads = layer_chain_oracle(g)
+    scale = lambda r: max(1.0, np.abs(r).max())  # noqa: E731
+    assert np.abs(out - g("out")).max() <= 1e-5 * scale(g("out"))
+    for name, got in grads.items():
+        ref = g(name)
+        assert np.abs(got - ref).max() <= 1e-5 * scale(ref), name
