@@ -678,6 +678,37 @@ def time_launches(device, fns, steps, warmup):
 RW_SWEEP = ((4, 1, 768, False), (4, 1, 768, True), (4, 2, 768, False), (4, 4, 512, False), (6, 3, 1024, True),
             (2, 1, 2048, False), (8, 4, 1024, False))
 
+def time_sinkhorn(device, B, n, iters, steps, warmup):
+    """Sinkhorn-Knopp fwd + bwd over B matrices: the two kernels through the
+    C-ABI, and for context the same op sequence as eager torch on the GPU
+    (exp, then iters x (row sum, divide, column sum, divide), autograd)."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(0)
+    H = (torch.randn(B, n, n, generator=g) + 2.0 * torch.eye(n)).to(device)
+    G = torch.randn(B, n, n, generator=g).to(device)
+    P, dH = torch.empty_like(H), torch.empty_like(H)
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    def kernels():
+        _lib.check(lib.hc_sinkhorn_fwd(H.data_ptr(), P.data_ptr(), B, n, iters, stream), "hc_sinkhorn_fwd")
+        _lib.check(lib.hc_sinkhorn_bwd(H.data_ptr(), G.data_ptr(), dH.data_ptr(), B, n, iters, stream),
+                   "hc_sinkhorn_bwd")
+
+    def eager():
+        h = H.detach().requires_grad_(True)
+        x = h.exp()
+        for _ in range(iters):
+            x = x / x.sum(dim=-1, keepdim=True)
+            x = x / x.sum(dim=-2, keepdim=True)
+        x.backward(G)
+
+    k_ms, e_ms = time_launches(device, [kernels, eager], steps, warmup)
+    return {"sweep": "sinkhorn", "batch": B, "n": n, "iters": iters, "kernels_ms": k_ms, "matrices_per_s": B / (k_ms * 1e-3),
+            "torch_eager_gpu_ms": e_ms}
+
+
 SWEEP_N = (2, 3, 4, 6, 8)
 SWEEP_D = (512, 1024, 2048, 4096)
 
@@ -685,8 +716,9 @@ SWEEP_D = (512, 1024, 2048, 4096)
 def run_sweep(args):
     """The small-n sweep at 16,384 tokens, bf16: one JSON line per (n, D) with
     the fused fwd+bwd GB/s and its fraction of the HBM peak; one line per
-    (n, m, D, projection) for the two-phase read / mix-write kernels; then one
-    line per n for the per-token batched expm (16,384 matrices, fwd+bwd)."""
+    (n, m, D, projection) for the two-phase read / mix-write kernels; the
+    Sinkhorn-Knopp projection at n = 2, 4, 8; then one line per n for the
+    per-token batched expm (16,384 matrices, fwd+bwd)."""
     _, _, local = dist_env()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -720,6 +752,9 @@ def run_sweep(args):
         line["frac_of_peak"] = line["gbs"] / peak
         print(json.dumps(line), flush=True)
         del r
+    for n in (2, 4, 8):
+        line = time_sinkhorn(device, TOKENS, n, 20, steps, args.warmup)
+        print(json.dumps(line), flush=True)
     for n in SWEEP_N:
         ms = float(np.mean(time_expm(device, steps, args.warmup, B=TOKENS, n=n)))
         print(json.dumps({"sweep": "expm_t18", "batch": TOKENS, "n": n, "ms_per_step": ms,

@@ -53,13 +53,15 @@ _SIGNATURES = {
         _c_int,
         [_vp] * 12 + [_c_i64, _c_int, _c_i64, _c_int, _vp],
     ),
+    "hc_sinkhorn_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _c_int, _vp]),
+    "hc_sinkhorn_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _vp]),
     "hc_read_fwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_read_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_fwd": (_c_int, [_vp] * 6 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_bwd": (_c_int, [_vp] * 11 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
 }
 
-EXPECTED_ABI_VERSION = 2
+EXPECTED_ABI_VERSION = 3
 
 _lib: Optional[ctypes.CDLL] = None
 _load_error: Optional[str] = None

@@ -1049,9 +1049,20 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   return true;
 }
 
+// Backward kernels with up to 12 warps: fewer consumers than the register
+// budget allows keep more stages loading (a consumer holds its stage while it
+// computes): 8 for whole tokens, 7 for sliced ones, measured best over n <= 4,
+// D in 512..4096 on B200.
+inline void prefer_bwd_consumers(WarpGeometry& geo) {
+  if (warp_tuning().warps > 0) return;
+  geo.consumers = std::min(geo.consumers, geo.ns > 1 ? 7 : 8);
+}
+
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
                           int num_sms) {
-  return ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms);
+  if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms)) return false;
+  if (bwd && warp_cap(bwd, n) > 8) prefer_bwd_consumers(geo);
+  return true;
 }
 
 template <typename KernelT>

@@ -39,7 +39,10 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
              bool streams_aligned) {
   const int es = dtype_size(sdt);
   if (!streams_aligned || !rw_ring_supported(n, m) || D % (16 / es) != 0) return false;
-  return ring_geometry(geo, rw_rows(bwd, n, m, mixw), rw_cap(bwd, n, m, mixw, proj), T, D, es, sm_count());
+  const int cap = rw_cap(bwd, n, m, mixw, proj);
+  if (!ring_geometry(geo, rw_rows(bwd, n, m, mixw), cap, T, D, es, sm_count())) return false;
+  if (bwd && cap > 8) prefer_bwd_consumers(geo);
+  return true;
 }
 
 }  // namespace

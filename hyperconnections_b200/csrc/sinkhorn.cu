@@ -1,0 +1,209 @@
+// sinkhorn.cu — batched Sinkhorn-Knopp projection of small matrices (n <= 8),
+// forward and backward, float32.
+//
+// Per matrix (reference hyperconnections/mhc.py:97-102, _sinkhorn_knopp):
+//   X_0 = exp(H)
+//   for k = 1..iters:  Y_k = X_{k-1} / rowsum(X_{k-1})     (each row sums to 1)
+//                      X_k = Y_k / colsum(Y_k)             (each column sums to 1)
+//   P = X_iters
+// Backward, given G = dL/dP, in reverse order of the steps:
+//   column step   dY_ij = (dX_ij - sum_l dX_lj X_lj) / c_j,  X_lj = Y_lj / c_j
+//   row step      dX_ij = (dY_ij - sum_l dY_il Y_il) / r_i
+//   exp           dH = dX_0 * X_0
+// (the autograd rules of the reference's divisions and sums, applied per step).
+//
+// One thread owns one matrix in registers. A CTA stages its 128 matrices
+// through shared memory so that global loads and stores are coalesced. The
+// backward recomputes the forward prefix X_{k-1} for each step k from X_0
+// (iters^2 / 2 half-steps, no stored iterates): at the reference's 20
+// iterations this is a few hundred n x n normalisations per matrix, all in
+// registers, instead of saving 40 intermediate matrices per token.
+#include "common.cuh"
+
+namespace hc {
+namespace {
+
+constexpr int kSkThreads = 128;
+constexpr int kSkMaxIters = 256;
+
+template <int N>
+__device__ __forceinline__ void row_normalize(float* x, float* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += x[i * N + j];
+    r[i] = s;
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[i * N + j] = x[i * N + j] / s;
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void col_normalize(float* x, float* c) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s += x[i * N + j];
+    c[j] = s;
+#pragma unroll
+    for (int i = 0; i < N; ++i) x[i * N + j] = x[i * N + j] / s;
+  }
+}
+
+// Shared-memory row of one matrix: N*N floats plus one pad word, so that the
+// threads of a warp (consecutive matrices) fall into different banks.
+template <int N> constexpr int sk_pitch() { return N * N + 1; }
+
+template <int N>
+__device__ __forceinline__ void stage_in(const float* __restrict__ g, float* sm, int64_t first, int cnt) {
+  const float* src = g + first * (N * N);
+  for (int i = threadIdx.x; i < cnt * N * N; i += blockDim.x) sm[(i / (N * N)) * sk_pitch<N>() + i % (N * N)] = src[i];
+}
+
+template <int N>
+__device__ __forceinline__ void stage_out(float* __restrict__ g, const float* sm, int64_t first, int cnt) {
+  float* dst = g + first * (N * N);
+  for (int i = threadIdx.x; i < cnt * N * N; i += blockDim.x) dst[i] = sm[(i / (N * N)) * sk_pitch<N>() + i % (N * N)];
+}
+
+template <int N>
+__global__ void __launch_bounds__(kSkThreads) sinkhorn_fwd_kernel(const float* __restrict__ H, float* __restrict__ P,
+                                                                  int64_t batch, int iters) {
+  __shared__ float sm[kSkThreads * sk_pitch<N>()];
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kSkThreads;
+  const int cnt = static_cast<int>(batch - first < kSkThreads ? batch - first : kSkThreads);
+  stage_in<N>(H, sm, first, cnt);
+  __syncthreads();
+  if (threadIdx.x < cnt) {
+    float* row = sm + threadIdx.x * sk_pitch<N>();
+    float x[N * N], r[N], c[N];
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) x[k] = expf(row[k]);
+    for (int it = 0; it < iters; ++it) {
+      row_normalize<N>(x, r);
+      col_normalize<N>(x, c);
+    }
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) row[k] = x[k];
+  }
+  __syncthreads();
+  stage_out<N>(P, sm, first, cnt);
+}
+
+template <int N>
+__global__ void __launch_bounds__(kSkThreads) sinkhorn_bwd_kernel(const float* __restrict__ H,
+                                                                  const float* __restrict__ G,
+                                                                  float* __restrict__ dH, int64_t batch, int iters) {
+  __shared__ float sm[kSkThreads * sk_pitch<N>()];
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kSkThreads;
+  const int cnt = static_cast<int>(batch - first < kSkThreads ? batch - first : kSkThreads);
+  float x0[N * N], g[N * N];
+  stage_in<N>(H, sm, first, cnt);
+  __syncthreads();
+  float* row = sm + threadIdx.x * sk_pitch<N>();
+  if (threadIdx.x < cnt) {
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) x0[k] = expf(row[k]);
+  }
+  __syncthreads();
+  stage_in<N>(G, sm, first, cnt);
+  __syncthreads();
+  if (threadIdx.x < cnt) {
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) g[k] = row[k];
+    for (int k = iters; k >= 1; --k) {
+      float y[N * N], r[N], c[N];
+#pragma unroll
+      for (int q = 0; q < N * N; ++q) y[q] = x0[q];
+      for (int it = 1; it < k; ++it) {  // X_{k-1}
+        row_normalize<N>(y, r);
+        col_normalize<N>(y, c);
+      }
+      row_normalize<N>(y, r);  // Y_k and its row sums r
+#pragma unroll
+      for (int j = 0; j < N; ++j) {  // column sums of Y_k
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) s += y[i * N + j];
+        c[j] = s;
+      }
+      // column step: dY_ij = (g_ij - sum_l g_lj X_lj) / c_j with X_lj = Y_lj / c_j
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float t = 0.f;
+#pragma unroll
+        for (int l = 0; l < N; ++l) t += g[l * N + j] * (y[l * N + j] / c[j]);
+#pragma unroll
+        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - t) / c[j];
+      }
+      // row step: dX_ij = (dY_ij - sum_l dY_il Y_il) / r_i
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float t = 0.f;
+#pragma unroll
+        for (int l = 0; l < N; ++l) t += g[i * N + l] * y[i * N + l];
+#pragma unroll
+        for (int j = 0; j < N; ++j) g[i * N + j] = (g[i * N + j] - t) / r[i];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < N * N; ++q) row[q] = g[q] * x0[q];
+  }
+  __syncthreads();
+  stage_out<N>(dH, sm, first, cnt);
+}
+
+int check_sk(const void* a, const void* b, int64_t batch, int n, int iters) {
+  if (batch < 0 || batch > (int64_t(1) << 37)) return HC_ERR_BAD_SIZE;
+  if (iters < 0 || iters > kSkMaxIters) return HC_ERR_BAD_SIZE;
+  if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
+  if (batch == 0) return HC_OK;
+  if (!a || !b) return HC_ERR_NULL_POINTER;
+  if (!aligned4(a) || !aligned4(b)) return HC_ERR_ALIGNMENT;
+  return HC_OK;
+}
+
+#define HC_SK_SWITCH(n, LAUNCH) \
+  switch (n) {                  \
+    case 1: LAUNCH(1); break;   \
+    case 2: LAUNCH(2); break;   \
+    case 3: LAUNCH(3); break;   \
+    case 4: LAUNCH(4); break;   \
+    case 5: LAUNCH(5); break;   \
+    case 6: LAUNCH(6); break;   \
+    case 7: LAUNCH(7); break;   \
+    case 8: LAUNCH(8); break;   \
+    default: return HC_ERR_UNSUPPORTED_N; \
+  }
+
+}  // namespace
+}  // namespace hc
+
+using namespace hc;
+
+extern "C" int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, int iters, void* stream) {
+  int rc = check_sk(H, P, batch, n, iters);
+  if (rc || batch == 0) return rc;
+  const unsigned grid = static_cast<unsigned>((batch + kSkThreads - 1) / kSkThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define L(NN) sinkhorn_fwd_kernel<NN><<<grid, kSkThreads, 0, st>>>(H, P, batch, iters)
+  HC_SK_SWITCH(n, L)
+#undef L
+  return launch_status();
+}
+
+extern "C" int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_t batch, int n, int iters,
+                               void* stream) {
+  int rc = check_sk(H, dH, batch, n, iters);
+  if (rc || batch == 0) return rc;
+  if (!G) return HC_ERR_NULL_POINTER;
+  if (!aligned4(G)) return HC_ERR_ALIGNMENT;
+  const unsigned grid = static_cast<unsigned>((batch + kSkThreads - 1) / kSkThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define L(NN) sinkhorn_bwd_kernel<NN><<<grid, kSkThreads, 0, st>>>(H, G, dH, batch, iters)
+  HC_SK_SWITCH(n, L)
+#undef L
+  return launch_status();
+}

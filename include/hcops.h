@@ -130,6 +130,18 @@ int hc_expm_pade_fwd(const float* A, float* E, int64_t batch, int n,
 int hc_expm_pade_bwd(const float* A, const float* G, float* dA, int64_t batch,
                      int n, void* stream);
 
+/* Sinkhorn-Knopp projection of exp(H) onto the doubly stochastic matrices:
+ * X = exp(H), then `iters` times: divide each row by its sum, then each
+ * column by its sum. H, P [batch, n, n] float32; 0 <= iters <= 256.
+ * Replaces: hyperconnections/mhc.py:97-102 (MHC._sinkhorn_knopp). */
+int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, int iters,
+                    void* stream);
+
+/* dH = gradient of sum(G * sinkhorn(H)) with respect to H, the reverse of
+ * every normalisation step (the autograd backward of mhc.py:97-102). */
+int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_t batch,
+                    int n, int iters, void* stream);
+
 /* ===========================================================================
  * stream_mix_add: out = Phi x + Y              (v == NULL)
  *                 out = Phi x + (v - Phi v)(v^T x) + Y   (v != NULL)

@@ -19,7 +19,8 @@ What runs, all from the reference checkout, unmodified:
   * one CGHC layer (cghc.py) per generator type and projection mode: its own
     read/write weights, generator, projection and forward output, with the
     gradients of its read -> module -> write -> matrix_exp -> mix chain
-    -> layer.npz.
+    -> layer.npz;
+  * MHC's Sinkhorn-Knopp method (mhc.py:97-102) with autograd -> sinkhorn.npz.
 
 The reference imports timm only for trunc_normal_; a stub providing
 torch.nn.init.trunc_normal_ is written to a temporary directory and put on
@@ -335,6 +336,30 @@ def gen_layer(ref_path, out):
     np.savez_compressed(os.path.join(out, "layer.npz"), **rec)
 
 
+def gen_sinkhorn(out):
+    """MHC's Sinkhorn-Knopp projection (mhc.py:97-102) run as the reference's
+    own method, float32, with autograd for the gradient."""
+    from types import SimpleNamespace
+
+    from hyperconnections.mhc import ManifoldHyperConnections as MHC
+
+    rec = {}
+    cases = [(64, 4, 20, 0.0), (37, 2, 20, 1.0), (50, 3, 5, 0.5), (16, 6, 20, 1.0), (16, 8, 20, 2.0), (9, 1, 3, 1.0),
+             (40, 4, 0, 1.0), (130, 4, 1, 1.0), (25, 5, 50, 3.0), (12, 7, 10, 1.0)]
+    for ci, (B, n, iters, scale) in enumerate(cases):
+        g = torch.Generator().manual_seed(5000 + ci)
+        H = scale * torch.randn(B, n, n, generator=g) + 2.0 * torch.eye(n)
+        G = torch.randn(B, n, n, generator=g)
+        Hr = H.clone().requires_grad_(True)
+        P = MHC._sinkhorn_knopp(SimpleNamespace(sinkhorn_iters=iters), Hr)
+        P.backward(G)
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([B, n, iters])
+        for name, t in (("H", H), ("G", G), ("P", P.detach()), ("dH", Hr.grad)):
+            rec[f"{key}_{name}"] = t.numpy()
+    np.savez_compressed(os.path.join(out, "sinkhorn.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -346,6 +371,7 @@ def main():
     gen_fused(ref_small, args.out)
     gen_rw(ref_small, args.out)
     gen_layer(args.reference, args.out)
+    gen_sinkhorn(args.out)
     for name in sorted(os.listdir(args.out)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")

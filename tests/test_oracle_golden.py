@@ -153,3 +153,18 @@ def test_oracle_cghc_layer_chain_matches_reference(case):
     for name, got in grads.items():
         ref = g(name)
         assert np.abs(got - ref).max() <= 1e-5 * scale(ref), name
+
+
+SINK = load_golden("sinkhorn.npz")
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in SINK}))
+def test_oracle_sinkhorn_matches_reference(case):
+    """MHC's Sinkhorn-Knopp method (mhc.py:97-102), forward and autograd backward."""
+    from oracle import sinkhorn as osk
+
+    g = lambda name: SINK[f"{case}_{name}"]  # noqa: E731
+    iters = int(g("meta")[2])
+    np.testing.assert_allclose(osk.sinkhorn_fwd(g("H"), iters), g("P"), rtol=1e-5, atol=1e-6)
+    dH = osk.sinkhorn_bwd(g("H"), g("G"), iters)
+    assert np.abs(dH - g("dH")).max() <= 1e-5 * max(1.0, np.abs(g("dH")).max())
