@@ -299,8 +299,9 @@ class ExpmRunner:
         self._check(rc, "hc_expm_t18_fwd")
 
     def bwd(self):
+        # mode 2: reuse the partial maxima of A that the forward left in scratch
         rc = self.lib.hc_expm_t18_bwd(self.A.data_ptr(), self.G.data_ptr(), self.dA.data_ptr(), self.B, self.n,
-                                      self.scratch.data_ptr(), self.words, 0, self.stream)
+                                      self.scratch.data_ptr(), self.words, 2, self.stream)
         self._check(rc, "hc_expm_t18_bwd")
 
 

@@ -61,7 +61,7 @@ _SIGNATURES = {
     "hc_mix_write_bwd": (_c_int, [_vp] * 11 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
 }
 
-EXPECTED_ABI_VERSION = 3
+EXPECTED_ABI_VERSION = 4
 
 _lib: Optional[ctypes.CDLL] = None
 _load_error: Optional[str] = None

@@ -632,6 +632,7 @@ extern "C" int64_t hc_expm_t18_scratch_words(int64_t batch, int n) {
 
 extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, float* scratch,
                                int64_t scratch_words, int per_matrix, void* stream) {
+  if (per_matrix != 0 && per_matrix != 1) return HC_ERR_BAD_SIZE;
   int rc = check(A, E, batch, n);
   if (rc || batch == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -654,6 +655,7 @@ extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, f
 
 extern "C" int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch, int n,
                                float* scratch, int64_t scratch_words, int per_matrix, void* stream) {
+  if (per_matrix < 0 || per_matrix > 2) return HC_ERR_BAD_SIZE;
   int rc = check(A, dA, batch, n);
   if (rc || batch == 0) return rc;
   if (!G) return HC_ERR_NULL_POINTER;
@@ -661,12 +663,14 @@ extern "C" int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* partial = nullptr;
   int parts = 0;
-  if (!per_matrix) {
+  if (per_matrix != 1) {
     parts = norm_parts(batch, n);
     if (!scratch || scratch_words < parts) return HC_ERR_SCRATCH;
     if (!aligned4(scratch)) return HC_ERR_ALIGNMENT;
-    rc = launch_norm_partials(A, batch, n, scratch, parts, st);
-    if (rc) return rc;
+    if (per_matrix == 0) {  // mode 2: the forward's partial maxima of this A are already in scratch
+      rc = launch_norm_partials(A, batch, n, scratch, parts, st);
+      if (rc) return rc;
+    }
     partial = scratch;
   }
   const dim3 grid = expm_grid(batch, n);

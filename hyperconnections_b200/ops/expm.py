@@ -59,6 +59,7 @@ class _ExpmT18Fn(torch.autograd.Function):
             )
         _lib.check(rc, "hc_expm_t18_fwd")
         ctx.save_for_backward(A32)
+        ctx.scratch = scratch  # the partial maxima of A, reused by the backward
         ctx.per_matrix = per_matrix
         ctx.shape = A.shape
         ctx.dtype = A.dtype
@@ -71,12 +72,12 @@ class _ExpmT18Fn(torch.autograd.Function):
         G = grad.to(torch.float32).contiguous().view(batch, n, n)
         dA = torch.empty_like(A32)
         lib = _lib.lib()
-        words = max(1, lib.hc_expm_t18_scratch_words(batch, n))
-        scratch = None if ctx.per_matrix else torch.empty(words, dtype=torch.float32, device=A32.device)
+        scratch = ctx.scratch
+        words = 0 if scratch is None else scratch.numel()
         with torch.cuda.device(A32.device):
             rc = lib.hc_expm_t18_bwd(
-                A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n, _lib.ptr(scratch),
-                words if scratch is not None else 0, 1 if ctx.per_matrix else 0, _lib.stream_of(A32),
+                A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n, _lib.ptr(scratch), words,
+                1 if ctx.per_matrix else 2, _lib.stream_of(A32),
             )
         _lib.check(rc, "hc_expm_t18_bwd")
         return dA.view(ctx.shape).to(ctx.dtype), None

@@ -92,7 +92,12 @@ int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n,
 
 /* dA = L_exp18(A^T, G): the adjoint Frechet derivative of the same T18
  * approximant (same scaling exponent as the forward), i.e. the gradient of
- * sum(G * expm_t18(A)) with respect to A.
+ * sum(G * expm_t18(A)) with respect to A. per_matrix: 0 global scaling (the
+ * partial maxima are recomputed into scratch), 1 per-matrix scaling, 2 global
+ * scaling reusing the partial maxima that hc_expm_t18_fwd left in `scratch`
+ * for this same A (saves one pass over A; the caller keeps scratch intact
+ * between the two calls). Any other value returns HC_ERR_BAD_SIZE, and so
+ * does a per_matrix other than 0 or 1 in hc_expm_t18_fwd.
  * Replaces: the autograd backward of hyperconnections/ops/expm.py:69-106. */
 int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch,
                     int n, float* scratch, int64_t scratch_words,

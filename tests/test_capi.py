@@ -78,6 +78,26 @@ def test_fused_and_expm_argument_checks():
     assert 1 <= words <= 1024
     assert lib.hc_expm_t18_fwd(FAKE, FAKE, 65536, 4, FAKE, words - 1, 0, None) == HC_ERR_SCRATCH
     assert lib.hc_expm_t18_scratch_words(10, 9) == 0
+    # scaling modes: fwd takes 0 / 1, bwd 0 / 1 / 2 (2 = reuse the forward's partial maxima)
+    assert lib.hc_expm_t18_fwd(FAKE, FAKE, 10, 4, FAKE, 1024, 2, None) == HC_ERR_SIZE
+    assert lib.hc_expm_t18_bwd(FAKE, FAKE, FAKE, 10, 4, FAKE, 1024, 3, None) == HC_ERR_SIZE
+    assert lib.hc_expm_t18_bwd(FAKE, FAKE, FAKE, 10, 4, None, 0, 2, None) == HC_ERR_SCRATCH
+
+
+def test_read_write_and_sinkhorn_argument_checks():
+    lib = _lib.lib()
+    assert lib.hc_read_fwd(FAKE, FAKE, FAKE, 4, 4, 5, 64, 2, None) == HC_ERR_N  # m > 4
+    assert lib.hc_read_fwd(FAKE, FAKE, FAKE, 4, 9, 1, 64, 2, None) == HC_ERR_N  # n > 8
+    assert lib.hc_read_fwd(None, FAKE, FAKE, 4, 4, 1, 64, 2, None) == HC_ERR_NULL
+    assert lib.hc_read_fwd(FAKE + 2, FAKE, FAKE, 4, 4, 1, 64, 2, None) == HC_ERR_ALIGN
+    assert lib.hc_read_bwd(FAKE, FAKE, FAKE, FAKE, FAKE, 4, 4, 1, 64, 7, None) == HC_ERR_DTYPE
+    assert lib.hc_mix_write_fwd(FAKE, FAKE, None, FAKE, None, FAKE, 4, 4, 2, 64, 2, None) == HC_ERR_NULL
+    assert lib.hc_mix_write_bwd(*([FAKE] * 11), -1, 4, 2, 64, 2, None) == HC_ERR_SIZE
+    assert lib.hc_mix_write_fwd(*([None] * 6), 0, 4, 2, 64, 2, None) == HC_OK  # empty: no work
+    assert lib.hc_sinkhorn_fwd(FAKE, FAKE, 10, 9, 20, None) == HC_ERR_N
+    assert lib.hc_sinkhorn_fwd(FAKE, FAKE, 10, 4, 257, None) == HC_ERR_SIZE
+    assert lib.hc_sinkhorn_bwd(FAKE, None, FAKE, 10, 4, 20, None) == HC_ERR_NULL
+    assert lib.hc_sinkhorn_fwd(None, None, 0, 4, 20, None) == HC_OK
 
 
 def test_cpu_tensors_raise_without_fallback():

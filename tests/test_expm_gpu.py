@@ -155,3 +155,27 @@ def test_errors():
         o.expm_t18(torch.zeros(2, 9, 9, device=DEVICE))
     with pytest.raises(ValueError):
         o.matrix_exp(torch.zeros(2, 3, 4, device=DEVICE))
+
+
+def test_t18_backward_reuses_forward_partial_maxima():
+    """hc_expm_t18_bwd mode 2 (the forward's partial maxima of A left in
+    scratch) gives exactly the result of mode 0 (recomputed)."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(5)
+    for batch, n in ((65536, 4), (3000, 7), (1, 2)):
+        A = (2.0 * torch.randn(batch, n, n, generator=g)).cuda()
+        G = torch.randn(batch, n, n, generator=g).cuda()
+        words = lib.hc_expm_t18_scratch_words(batch, n)
+        scratch = torch.empty(words, device="cuda")
+        E, d0, d2 = torch.empty_like(A), torch.empty_like(A), torch.empty_like(A)
+        s = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.hc_expm_t18_bwd(A.data_ptr(), G.data_ptr(), d0.data_ptr(), batch, n, scratch.data_ptr(),
+                                       words, 0, s), "bwd mode 0")
+        scratch.fill_(float("nan"))  # mode 2 must read what the forward writes
+        _lib.check(lib.hc_expm_t18_fwd(A.data_ptr(), E.data_ptr(), batch, n, scratch.data_ptr(), words, 0, s), "fwd")
+        _lib.check(lib.hc_expm_t18_bwd(A.data_ptr(), G.data_ptr(), d2.data_ptr(), batch, n, scratch.data_ptr(),
+                                       words, 2, s), "bwd mode 2")
+        torch.cuda.synchronize()
+        assert torch.equal(d0, d2)
