@@ -4,6 +4,7 @@
 // dtype codes, NULL pointers and alignment. The 16-byte vector path is taken
 // when D is a multiple of the chunk width and every stream base pointer is
 // 16-byte aligned; otherwise the element-wise path of the same kernels runs.
+#include "bign.cuh"
 #include "rw_warp.cuh"
 
 namespace hc {
@@ -18,11 +19,29 @@ int check_dtypes(int sdt, int pdt) {
   return HC_OK;
 }
 
-int check_sizes(int64_t T, int n, int64_t D) {
+int check_sizes(int64_t T, int n, int64_t D, int max_n = 8) {
   // one CTA row per token: the grid must stay within 2^31 - 1 CTAs
   if (T < 0 || T > kMaxTokens || D < 0 || D > kMaxD) return HC_ERR_BAD_SIZE;
-  if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
+  if (n < 1 || n > max_n) return HC_ERR_UNSUPPORTED_N;
   return HC_OK;
+}
+
+int run_big_fwd(int sdt, bool proj, bool vec, bool pf32, int n, const MixFwdArgs& a, cudaStream_t s) {
+  switch (sdt) {
+    case HC_DTYPE_F32: return big_fwd_f32(proj, vec, pf32, n, a, s);
+    case HC_DTYPE_F16: return big_fwd_f16(proj, vec, pf32, n, a, s);
+    case HC_DTYPE_BF16: return big_fwd_bf16(proj, vec, pf32, n, a, s);
+  }
+  return HC_ERR_DTYPE;
+}
+
+int run_big_bwd(int sdt, bool proj, bool pf32, int n, const MixBwdArgs& a, cudaStream_t s) {
+  switch (sdt) {
+    case HC_DTYPE_F32: return big_bwd_f32(proj, false, pf32, n, a, s);
+    case HC_DTYPE_F16: return big_bwd_f16(proj, false, pf32, n, a, s);
+    case HC_DTYPE_BF16: return big_bwd_bf16(proj, false, pf32, n, a, s);
+  }
+  return HC_ERR_DTYPE;
 }
 
 int vec_width(int sdt) { return sdt == HC_DTYPE_F32 ? 4 : 8; }
@@ -83,13 +102,21 @@ using namespace hc;
 extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, const void* v,
                                  void* out, int64_t B, int n, int64_t D, int stream_dtype,
                                  int param_dtype, void* stream) {
-  int rc = check_sizes(B, n, D);
+  int rc = check_sizes(B, n, D, kBigMaxN);
   if (rc) return rc;
   rc = check_dtypes(stream_dtype, param_dtype);
   if (rc) return rc;
   if (B == 0 || D == 0) return HC_OK;
   if (!Phi || !x || !Y || !out) return HC_ERR_NULL_POINTER;
   if (!params_aligned(param_dtype, Phi) || !params_aligned(param_dtype, v)) return HC_ERR_ALIGNMENT;
+  if (n > 8) {  // shared-memory kernels; 32-bit word accesses when every row is word-aligned
+    MixFwdArgs a{};
+    a.x = x; a.src = Y; a.phi = Phi; a.v = v; a.out = out; a.T = B; a.D = D;
+    const bool word = stream_dtype == HC_DTYPE_F32 ||
+                      (D % 2 == 0 && aligned4(x) && aligned4(Y) && aligned4(out));
+    return run_big_fwd(stream_dtype, v != nullptr, word, param_dtype == HC_DTYPE_F32, n, a,
+                       static_cast<cudaStream_t>(stream));
+  }
   const int W = vec_width(stream_dtype);
   const bool vec = (D % W == 0) && aligned16(x) && aligned16(Y) && aligned16(out);
   const MixGeometry g = mix_geometry(B, D, vec ? W : 1);
@@ -107,7 +134,7 @@ extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, 
 extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, const void* v,
                                  void* grad_x, float* grad_Phi, float* grad_v, int64_t B, int n,
                                  int64_t D, int stream_dtype, int param_dtype, void* stream) {
-  int rc = check_sizes(B, n, D);
+  int rc = check_sizes(B, n, D, kBigMaxN);
   if (rc) return rc;
   rc = check_dtypes(stream_dtype, param_dtype);
   if (rc) return rc;
@@ -117,6 +144,14 @@ extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, 
   if (!params_aligned(param_dtype, Phi) || !params_aligned(param_dtype, v)) return HC_ERR_ALIGNMENT;
   if ((grad_Phi && !aligned4(grad_Phi)) || (grad_v && !aligned4(grad_v))) return HC_ERR_ALIGNMENT;
   if (v == nullptr) grad_v = nullptr;
+  if (n > 8) {  // D == 0 still writes the (all-zero) parameter gradients
+    MixBwdArgs a{};
+    a.g = G; a.x = x; a.phi = Phi; a.v = v;
+    a.grad_x = D > 0 ? grad_x : nullptr; a.grad_phi = grad_Phi; a.grad_v = grad_v;
+    a.T = B; a.D = D;
+    return run_big_bwd(stream_dtype, v != nullptr, param_dtype == HC_DTYPE_F32, n, a,
+                       static_cast<cudaStream_t>(stream));
+  }
   const int W = vec_width(stream_dtype);
   const bool vec = (D % W == 0) && aligned16(G) && aligned16(x) && (grad_x == nullptr || aligned16(grad_x));
   const MixGeometry g = mix_geometry(B, D, vec ? W : 1);

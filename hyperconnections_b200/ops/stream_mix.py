@@ -31,7 +31,8 @@ HAS_TRITON = _lib.available()
 """Name kept from the reference (ops/__init__.py:1); here it means that the
 sm_100a kernels of libhcops.so are available."""
 
-MAX_STREAMS = 8
+MAX_STREAMS = 8       # the fused step and the m-block read / mix-write
+MAX_STREAMS_ADD = 32  # stream_mix_add: n <= 8 register kernels, 9..32 shared-memory kernels
 
 
 def _param_dtype(Phi: torch.Tensor, v: torch.Tensor | None, x: torch.Tensor) -> torch.dtype:
@@ -119,6 +120,6 @@ def stream_mix_add(
         assert v.shape == (B, N)
     if not (Phi.is_cuda and Y.is_cuda and (v is None or v.is_cuda)):
         raise RuntimeError("stream_mix_add requires CUDA tensors")
-    if N > MAX_STREAMS:
-        raise RuntimeError(f"stream_mix_add supports N <= {MAX_STREAMS} streams, got N={N}")
+    if N > MAX_STREAMS_ADD:
+        raise RuntimeError(f"stream_mix_add supports N <= {MAX_STREAMS_ADD} streams, got N={N}")
     return _StreamMixFn.apply(Phi, x, Y, v)

@@ -37,7 +37,7 @@ extern "C" {
 #define HC_OK                 0
 #define HC_ERR_NULL_POINTER   1  /* a required pointer is NULL                     */
 #define HC_ERR_BAD_SIZE       2  /* negative size, or n / D out of range           */
-#define HC_ERR_UNSUPPORTED_N  3  /* n outside 1..8 (or m outside 1..4)            */
+#define HC_ERR_UNSUPPORTED_N  3  /* n (or m) outside the entry point's range      */
 #define HC_ERR_DTYPE          4  /* unknown dtype code or unsupported combination  */
 #define HC_ERR_ALIGNMENT      5  /* a float32 pointer is not 4-byte aligned        */
 #define HC_ERR_SCRATCH        6  /* scratch buffer missing or too small            */
@@ -154,7 +154,9 @@ int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_t batch,
  * HC_DTYPE_F32 or equal to stream_dtype. fp32 accumulation.
  * ======================================================================== */
 
-/* Replaces: hyperconnections/ops/stream_mix.py:57-86 (stream_mix_add) ->
+/* 1 <= n <= 32: n <= 8 runs the register kernels, 9..32 the shared-memory
+ * kernels (one CTA per token). Other entry points keep n <= 8.
+ * Replaces: hyperconnections/ops/stream_mix.py:57-86 (stream_mix_add) ->
  * stream_mix_small_nb.py:75-132 (_stream_mix_fwd) and
  * stream_mix_big_nb.py:74-146 (_stream_mix_fwd_big_nb). */
 int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y,

@@ -10,7 +10,7 @@ What runs, all from the reference checkout, unmodified:
   * torch.linalg.matrix_exp, which CGHC calls (cghc.py:321) -> matrix_exp.npz;
   * the reference's Triton stream-mix kernels and autograd Function
     (ops/stream_mix_small_nb.py) under TRITON_INTERPRET=1 with a fixed BLOCK_D
-    (the autotuner needs a GPU) -> stream_mix_*.npz;
+    (the autotuner needs a GPU) -> stream_mix_*.npz (N = 1..32);
   * CGHC's composition read einsum (cghc.py:410) -> write einsum (:417) ->
     stream_mix_add (:449, the small-NB Function) in float32 on bf16-exact
     inputs, forward and backward -> fused.npz;
@@ -193,6 +193,33 @@ def gen_stream_mix(ref_small, out):
     np.savez_compressed(os.path.join(out, "stream_mix_f16.npz"), **rec16)
 
 
+def gen_stream_mix_large_n(ref_small, out):
+    """stream_mix_add at 9 <= N <= 32 through the reference's small-NB Function
+    (the kernel stream_mix_add runs below the big-NB size threshold,
+    ops/stream_mix.py:45-51), float32, with and without projection."""
+    fn = ref_small.stream_mix_add_small_nb
+    cases = [(2, 12, 40, False), (2, 12, 40, True), (1, 16, 96, False), (2, 16, 33, True), (1, 32, 64, True),
+             (1, 9, 17, False), (1, 24, 48, True)]
+    rec = {}
+    for ci, (B, N, D, proj) in enumerate(cases):
+        Phi, x, Y = _make_inputs(B, N, D, torch.float32, seed=6000 + ci)
+        v = _make_v(B, N, torch.float32, seed=6100 + ci) if proj else None
+        g = torch.Generator().manual_seed(6200 + ci)
+        Gup = torch.randn(B, N, D, generator=g)
+        P, X, Yr = (t.clone().requires_grad_(True) for t in (Phi, x, Y))
+        Vr = v.clone().requires_grad_(True) if proj else None
+        o = fn(P, X, Yr, Vr)
+        o.backward(Gup)
+        key = f"c{ci}"
+        rec[f"{key}_meta"] = np.array([B, N, D, int(proj)])
+        items = [("Phi", Phi), ("x", x), ("Y", Y), ("Gup", Gup), ("out", o.detach()), ("gPhi", P.grad), ("gx", X.grad)]
+        if proj:
+            items += [("v", v), ("gv", Vr.grad)]
+        for name, t in items:
+            rec[f"{key}_{name}"] = t.numpy()
+    np.savez_compressed(os.path.join(out, "stream_mix_large_n.npz"), **rec)
+
+
 def gen_fused(ref_small, out):
     """CGHC composition (cghc.py:410, :417, :449) with m = 1, float32 math on
     bf16-exact inputs drawn like the fused-step workload."""
@@ -368,6 +395,7 @@ def main():
     ref_expm, ref_small = _import_reference(args.reference)
     gen_expm(ref_expm, args.out)
     gen_stream_mix(ref_small, args.out)
+    gen_stream_mix_large_n(ref_small, args.out)
     gen_fused(ref_small, args.out)
     gen_rw(ref_small, args.out)
     gen_layer(args.reference, args.out)

@@ -51,7 +51,7 @@ FAKE = 0x1000  # never dereferenced: every call below fails host-side checks
 @pytest.mark.parametrize(
     "args,want",
     [
-        ((FAKE, FAKE, FAKE, None, FAKE, 4, 9, 64, 2, 2, None), HC_ERR_N),
+        ((FAKE, FAKE, FAKE, None, FAKE, 4, 33, 64, 2, 2, None), HC_ERR_N),  # n <= 32
         ((FAKE, FAKE, FAKE, None, FAKE, 4, 0, 64, 2, 2, None), HC_ERR_N),
         ((FAKE, FAKE, FAKE, None, FAKE, -1, 4, 64, 2, 2, None), HC_ERR_SIZE),
         ((FAKE, FAKE, FAKE, None, FAKE, 4, 4, -5, 2, 2, None), HC_ERR_SIZE),

@@ -168,3 +168,19 @@ def test_oracle_sinkhorn_matches_reference(case):
     np.testing.assert_allclose(osk.sinkhorn_fwd(g("H"), iters), g("P"), rtol=1e-5, atol=1e-6)
     dH = osk.sinkhorn_bwd(g("H"), g("G"), iters)
     assert np.abs(dH - g("dH")).max() <= 1e-5 * max(1.0, np.abs(g("dH")).max())
+
+
+MIXL = load_golden("stream_mix_large_n.npz")
+
+
+@pytest.mark.parametrize("case", sorted({k.split("_")[0] for k in MIXL}))
+def test_oracle_stream_mix_large_n_matches_reference(case):
+    g = lambda name: MIXL[f"{case}_{name}"]  # noqa: E731
+    proj = bool(g("meta")[3])
+    v = g("v") if proj else None
+    np.testing.assert_allclose(omix.stream_mix_fwd(g("Phi"), g("x"), g("Y"), v), g("out"), rtol=1e-5, atol=1e-5)
+    gP, gx, _, gv = omix.stream_mix_bwd(g("Gup"), g("Phi"), g("x"), v)
+    np.testing.assert_allclose(gP, g("gPhi"), rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(gx, g("gx"), rtol=1e-4, atol=1e-4)
+    if proj:
+        np.testing.assert_allclose(gv, g("gv"), rtol=1e-4, atol=1e-4)

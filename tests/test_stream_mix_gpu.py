@@ -223,8 +223,8 @@ class TestEdgeCases:
             stream_mix_add(torch.randn(2, 4, 4), torch.randn(2, 4, 64), torch.randn(2, 4, 64))
 
     def test_too_many_streams_raises(self):
-        Phi, x, Y = make_inputs(2, 9, 16)
-        with pytest.raises(RuntimeError, match="N <= 8"):
+        Phi, x, Y = make_inputs(2, 33, 16)
+        with pytest.raises(RuntimeError, match="N <= 32"):
             stream_mix_add(Phi, x, Y)
 
     def test_large_D(self):
