@@ -175,7 +175,7 @@ struct WarpGeometry {
 // registers per thread) for n <= 4; the packed-pair backward for n <= 4 needs
 // up to 170 registers, so 12 warps; larger n use 8 warps (255 registers).
 constexpr int fwd_warp_cap(int n) { return n <= 4 ? 16 : 8; }
-constexpr int bwd_warp_cap(int n) { return n <= 4 ? 12 : 8; }
+constexpr int bwd_warp_cap(int n) { return n <= 6 ? 12 : 8; }
 constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap(n) : fwd_warp_cap(n); }
 
 // Issue the bulk copies of one item (cnt consecutive tokens, or one slice of
@@ -1017,12 +1017,14 @@ WarpTuning& warp_tuning();
 //   * tokens smaller than the item target are grouped, tpi per item, so that
 //     one bulk copy per tensor moves several tokens.
 inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
-                          int num_sms) {
+                          int num_sms, bool bwd) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
   const WarpTuning tune = warp_tuning();
   const int budget = 200 * 1024;
   const int64_t max_stage = 24 * 1024;
-  const int64_t item_target = tune.stage_bytes > 0 ? tune.stage_bytes : 12 * 1024;
+  // items of several small tokens: one bulk copy has a fixed cost, so small
+  // items cap the copy rate (12 KB forward, 16 KB backward measured best)
+  const int64_t item_target = tune.stage_bytes > 0 ? tune.stage_bytes : (bwd ? 16 : 12) * 1024;
   const int64_t tok_bytes = static_cast<int64_t>(rows) * D * esize;
   int64_t sl = D;
   int tpi = 1;
@@ -1051,17 +1053,21 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
 
 // Backward kernels with up to 12 warps: fewer consumers than the register
 // budget allows keep more stages loading (a consumer holds its stage while it
-// computes): 8 for whole tokens, 7 for sliced ones, measured best over n <= 4,
-// D in 512..4096 on B200.
-inline void prefer_bwd_consumers(WarpGeometry& geo) {
+// computes). Measured best on B200 over D in 512..4096: 7 for sliced tokens;
+// for whole tokens 8 at n <= 4 and all 11 at n = 5, 6.
+inline void prefer_bwd_consumers(WarpGeometry& geo, int n) {
   if (warp_tuning().warps > 0) return;
-  geo.consumers = std::min(geo.consumers, geo.ns > 1 ? 7 : 8);
+  if (geo.ns > 1) {
+    geo.consumers = std::min(geo.consumers, 7);
+  } else if (n <= 4) {
+    geo.consumers = std::min(geo.consumers, 8);
+  }
 }
 
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
                           int num_sms) {
-  if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms)) return false;
-  if (bwd && warp_cap(bwd, n) > 8) prefer_bwd_consumers(geo);
+  if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
+  if (bwd && warp_cap(bwd, n) > 8) prefer_bwd_consumers(geo, n);
   return true;
 }
 
@@ -1073,9 +1079,10 @@ inline int warp_prepare(KernelT* kernel, int smem_bytes) {
 }
 
 // 32-bit words per lane access: 16-byte accesses for the forward at n <= 4,
-// 8-byte accesses elsewhere (register budget).
+// 8-byte accesses elsewhere; 4-byte accesses for the backward at n = 5, 6,
+// which then fits 12 warps without spilling (register budget).
 constexpr int fwd_lane_words(int n) { return n <= 4 ? 4 : 2; }
-constexpr int kWarpW = 2;
+constexpr int bwd_lane_words(int n) { return (n == 5 || n == 6) ? 1 : 2; }
 
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cudaStream_t s) {
@@ -1101,7 +1108,7 @@ int launch_mix_bwd_warp(int n, const WarpGeometry& geo, const MixBwdArgs& a, cud
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
-    auto* k = mix_bwd_warp_kernel<T, P, NN, FUSED, PROJ, kWarpW>;       \
+    auto* k = mix_bwd_warp_kernel<T, P, NN, FUSED, PROJ, bwd_lane_words(NN)>; \
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;            \
     k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);                  \
     break;                                                              \
