@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kBigThreads) big_fwd_kernel(const MixFwdArgs a
 // Backward geometry: slice length of the staged rows, its row pitch (padded
 // against bank conflicts between rows) and the Gram tiling.
 template <int NMAX> struct BigBwd {
-  static constexpr int SL = NMAX <= 16 ? 512 : 256;   // elements per staged slice
+  static constexpr int SL = 256;                      // elements per staged slice
   static constexpr int EPT = SL / kBigThreads;        // elements per thread per row
   static constexpr int PITCH = SL + 4;
   static constexpr int ROWS = NMAX + 4;               // n + augmented row, padded to a tile multiple
