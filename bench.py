@@ -710,6 +710,53 @@ def time_sinkhorn(device, B, n, iters, steps, warmup):
             "torch_eager_gpu_ms": e_ms}
 
 
+# The reference's published stream_mix_add forward numbers (A100 80GB PCIe,
+# benchmarks/stream_mix_bench.py -> benchmark_small_n_exhaustive_4_3_2026.log):
+# (tokens B, N, D, dtype, projection, GB/s in the reference's byte model, log line)
+PUBLISHED_FWD = (
+    (2048, 4, 1024, "fp32", False, 947.2, 2129),
+    (2048, 4, 1024, "fp32", True, 967.4, 2130),
+    (2048, 4, 768, "fp32", False, 489.4, 2127),
+    (2048, 8, 1024, "fp32", False, 1031.8, 2169),
+    (2048, 16, 1536, "fp32", False, 1542.1, 2211),
+    (2048, 4, 768, "fp16", False, 244.9, 2248),
+    (2048, 4, 1024, "fp16", False, 248.3, 2250),
+    (2048, 8, 1024, "fp16", False, 923.0, 2290),
+)
+
+
+def reference_model_bytes(B, N, D, elem, proj):
+    """The reference benchmark's byte model (stream_mix_bench.py:329-336)."""
+    return elem * (B * N * N + 3 * B * N * D + (B * N if proj else 0))
+
+
+def time_stream_mix(device, B, N, D, dtype, proj, steps, warmup):
+    """stream_mix_add forward and backward through the C-ABI on resident
+    buffers, 256 MiB write flush between steps (as do_bench does)."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(0)
+    Phi = torch.randn(B, N, N, generator=g).to(dtype).to(device)
+    x, Y, G = (torch.randn(B, N, D, generator=g).to(dtype).to(device) for _ in range(3))
+    v = torch.nn.functional.normalize(torch.randn(B, N, generator=g), dim=-1).to(dtype).to(device) if proj else None
+    out, gx = torch.empty_like(x), torch.empty_like(x)
+    gP = torch.empty(B, N, N, device=device)
+    gv = torch.empty(B, N, device=device) if proj else None
+    code = _lib.dtype_code(dtype)
+    st = torch.cuda.current_stream(device).cuda_stream
+
+    def fwd():
+        _lib.check(lib.hc_stream_mix_fwd(Phi.data_ptr(), x.data_ptr(), Y.data_ptr(), _lib.ptr(v), out.data_ptr(),
+                                         B, N, D, code, code, st), "hc_stream_mix_fwd")
+
+    def bwd():
+        _lib.check(lib.hc_stream_mix_bwd(G.data_ptr(), Phi.data_ptr(), x.data_ptr(), _lib.ptr(v), gx.data_ptr(),
+                                         gP.data_ptr(), _lib.ptr(gv), B, N, D, code, code, st), "hc_stream_mix_bwd")
+
+    return time_launches(device, [fwd, bwd], steps, warmup)
+
+
 SWEEP_N = (2, 3, 4, 6, 8)
 SWEEP_D = (512, 1024, 2048, 4096)
 
@@ -739,6 +786,16 @@ def run_sweep(args):
                 "fwd_gbs": fb / (fwd_ms * 1e-3) / 1e9, "bwd_gbs": bb / (bwd_ms * 1e-3) / 1e9, "gbs": gbs,
                 "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": peak_kind,
                 "pct_of_8tbs": 100.0 * gbs / NOMINAL_HBM_GBS, "bytes": fb + bb}), flush=True)
+    dt = {"fp32": torch.float32, "fp16": torch.float16}
+    for B, N, D, name, proj, ref_gbs, line_no in PUBLISHED_FWD:
+        fwd_ms, bwd_ms = time_stream_mix(device, B, N, D, dt[name], proj, steps, args.warmup)
+        elem = 4 if name == "fp32" else 2
+        gbs = reference_model_bytes(B, N, D, elem, proj) / (fwd_ms * 1e-3) / 1e9
+        print(json.dumps({"sweep": "stream_mix_add_published", "tokens": B, "n": N, "D": D, "dtype": name,
+                          "proj": proj, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "fwd_gbs_reference_model": gbs,
+                          "reference_a100_gbs": ref_gbs, "ratio": gbs / ref_gbs,
+                          "reference_source": f"benchmark_small_n_exhaustive_4_3_2026.log:{line_no}"}),
+              flush=True)
     for n, m, D, proj in RW_SWEEP:
         r = RwRunner(device, TOKENS, n, m, D, proj)
         names = ("read_fwd", "read_bwd", "mix_write_fwd", "mix_write_bwd")
