@@ -55,13 +55,15 @@ _SIGNATURES = {
     ),
     "hc_sinkhorn_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _c_int, _vp]),
     "hc_sinkhorn_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _vp]),
+    "hc_cghc_generator_fwd": (_c_int, [_vp] * 7 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
+    "hc_cghc_generator_bwd": (_c_int, [_vp] * 13 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
     "hc_read_fwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_read_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_fwd": (_c_int, [_vp] * 6 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_bwd": (_c_int, [_vp] * 11 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
 }
 
-EXPECTED_ABI_VERSION = 4
+EXPECTED_ABI_VERSION = 5
 
 _lib: Optional[ctypes.CDLL] = None
 _load_error: Optional[str] = None

@@ -15,4 +15,4 @@ extern "C" const char* hc_error_string(int code) {
   }
 }
 
-extern "C" int hc_abi_version(void) { return 4; }
+extern "C" int hc_abi_version(void) { return 5; }

@@ -147,6 +147,31 @@ int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, int iters,
 int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_t batch,
                     int n, int iters, void* stream);
 
+/* CGHC's generator A per token, from the module's pre-activations (float32):
+ *   M = conserv_A + conv_pred(x) [T,n,n], lc = log_dt_conserv + dt_proj_conserv(x)
+ *   [T,n_dt], R = diss_A + diss_pred(x) [T,n,n], dpre = diss_diag + diss_pred(x)
+ *   [T,n], S = laplacian_A + laplacian_pred(x) [T,n,n], ld = log_dt_diss +
+ *   dt_proj_diss(x) [T,n_dt]; n_dt = n if vec_dt else 1.
+ * flags: 1 conservative, 2 PSD, 4 diagonal, 8 Laplacian dissipation (the
+ * seven generator types are the combinations the reference allows); inputs of
+ * absent terms may be NULL. A [T,n,n].
+ * Replaces: hyperconnections/cghc.py:219-315 (compute_generator) after its
+ * Linear layers. */
+int hc_cghc_generator_fwd(const float* M, const float* lc, const float* R,
+                          const float* dpre, const float* S, const float* ld,
+                          float* A, int64_t T, int n, int vec_dt, int flags,
+                          float dt_min_c, float dt_max_c, float dt_min_d,
+                          float dt_max_d, void* stream);
+
+/* Given G = dL/dA [T,n,n]: the gradients with respect to each pre-activation
+ * (same shapes as the inputs; any may be NULL to skip it). */
+int hc_cghc_generator_bwd(const float* M, const float* lc, const float* R,
+                          const float* dpre, const float* S, const float* ld,
+                          const float* G, float* dM, float* dlc, float* dR,
+                          float* ddpre, float* dS, float* dld, int64_t T, int n,
+                          int vec_dt, int flags, float dt_min_c, float dt_max_c,
+                          float dt_min_d, float dt_max_d, void* stream);
+
 /* ===========================================================================
  * stream_mix_add: out = Phi x + Y              (v == NULL)
  *                 out = Phi x + (v - Phi v)(v^T x) + Y   (v != NULL)

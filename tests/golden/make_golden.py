@@ -20,7 +20,9 @@ What runs, all from the reference checkout, unmodified:
     read/write weights, generator, projection and forward output, with the
     gradients of its read -> module -> write -> matrix_exp -> mix chain
     -> layer.npz;
-  * MHC's Sinkhorn-Knopp method (mhc.py:97-102) with autograd -> sinkhorn.npz.
+  * MHC's Sinkhorn-Knopp method (mhc.py:97-102) with autograd -> sinkhorn.npz;
+  * CGHC's compute_generator (cghc.py:219-315) for every generator type and
+    dt mode, its Linear outputs captured by hooks -> generator.npz.
 
 The reference imports timm only for trunc_normal_; a stub providing
 torch.nn.init.trunc_normal_ is written to a temporary directory and put on
@@ -363,6 +365,75 @@ def gen_layer(ref_path, out):
     np.savez_compressed(os.path.join(out, "layer.npz"), **rec)
 
 
+def gen_generator(out):
+    """CGHC's generator (cghc.py:219-315) for every generator type, scalar and
+    per-stream dt, computed by the reference layer's own compute_generator
+    with autograd. Forward hooks capture its Linear outputs; the fixture
+    stores the pre-activations the kernel takes (static parameter + Linear
+    output), the generator A, an upstream gradient and the gradients of the
+    Linear outputs (equal to those of the pre-activations)."""
+    from hyperconnections.cghc import ContinuousGenHyperConnections as CGHC
+
+    types = ["conservative", "psd_diss", "diagonal_diss", "laplacian", "conservative_diag_diss",
+             "conservative_psd_diss", "conservative_laplacian"]
+    configs = [(4, t, v) for t in types for v in (False, True)] + [(2, "conservative_psd_diss", True),
+                                                                   (6, "conservative_laplacian", False),
+                                                                   (8, "conservative_psd_diss", True),
+                                                                   (3, "conservative_diag_diss", True)]
+    rec = {}
+    for ci, (n, gen, vec) in enumerate(configs):
+        torch.manual_seed(7000 + ci)
+        block, m = 8, 1
+        layer = CGHC(n, m, n * block, m * block, torch.nn.Identity(), dt=0.3, generator_type=gen, vec_dt=vec,
+                     use_triton=False)
+        with torch.no_grad():
+            for name, prm in layer.named_parameters():
+                if prm.dim() >= 1:
+                    prm.add_(0.5 * torch.randn_like(prm))
+        captured = {}
+
+        def hook(name):
+            def fn(_mod, _inp, outp):
+                outp.retain_grad()
+                captured[name] = outp
+            return fn
+
+        for name in ("conv_pred", "dt_proj_conserv", "dt_proj_diss", "diss_pred", "laplacian_pred"):
+            if hasattr(layer, name):
+                getattr(layer, name).register_forward_hook(hook(name))
+        T = 20
+        x = torch.randn(T, n, block)
+        A = layer.compute_generator(x)
+        G = torch.randn(T, n, n)
+        A.backward(G)
+        key = f"c{ci}"
+        has_diss = any(hasattr(layer, k) for k in ("diss_A", "diss_diag", "laplacian_A"))
+        rec[f"{key}_meta"] = np.array([n, int(vec), T])
+        rec[f"{key}_type"] = np.array(gen)
+        rec[f"{key}_ranges"] = np.array([layer.dt_min_cons, layer.dt_max_cons, layer.dt_min_diss, layer.dt_max_diss])
+        rec[f"{key}_A"] = A.detach().numpy()
+        rec[f"{key}_G"] = G.numpy()
+        with torch.no_grad():
+            if hasattr(layer, "conserv_A"):
+                rec[f"{key}_M"] = (layer.conserv_A + captured["conv_pred"].reshape(T, n, n)).numpy()
+                rec[f"{key}_dM"] = captured["conv_pred"].grad.reshape(T, n, n).numpy()
+                rec[f"{key}_lc"] = (layer.log_dt_conserv + captured["dt_proj_conserv"]).numpy()
+                rec[f"{key}_dlc"] = captured["dt_proj_conserv"].grad.numpy()
+            if has_diss:
+                rec[f"{key}_ld"] = (layer.log_dt_diss + captured["dt_proj_diss"]).numpy()
+                rec[f"{key}_dld"] = captured["dt_proj_diss"].grad.numpy()
+            if hasattr(layer, "diss_A"):
+                rec[f"{key}_R"] = (layer.diss_A + captured["diss_pred"].reshape(T, n, n)).numpy()
+                rec[f"{key}_dR"] = captured["diss_pred"].grad.reshape(T, n, n).numpy()
+            if hasattr(layer, "diss_diag"):
+                rec[f"{key}_dpre"] = (layer.diss_diag + captured["diss_pred"]).numpy()
+                rec[f"{key}_ddpre"] = captured["diss_pred"].grad.numpy()
+            if hasattr(layer, "laplacian_A"):
+                rec[f"{key}_S"] = (layer.laplacian_A + captured["laplacian_pred"].reshape(T, n, n)).numpy()
+                rec[f"{key}_dS"] = captured["laplacian_pred"].grad.reshape(T, n, n).numpy()
+    np.savez_compressed(os.path.join(out, "generator.npz"), **rec)
+
+
 def gen_sinkhorn(out):
     """MHC's Sinkhorn-Knopp projection (mhc.py:97-102) run as the reference's
     own method, float32, with autograd for the gradient."""
@@ -400,6 +471,7 @@ def main():
     gen_rw(ref_small, args.out)
     gen_layer(args.reference, args.out)
     gen_sinkhorn(args.out)
+    gen_generator(args.out)
     for name in sorted(os.listdir(args.out)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")

@@ -184,3 +184,33 @@ def test_oracle_stream_mix_large_n_matches_reference(case):
     np.testing.assert_allclose(gx, g("gx"), rtol=1e-4, atol=1e-4)
     if proj:
         np.testing.assert_allclose(gv, g("gv"), rtol=1e-4, atol=1e-4)
+
+
+GEN = load_golden("generator.npz")
+GEN_CASES = sorted({k.split("_")[0] for k in GEN})
+GEN_INPUTS = ("M", "lc", "R", "dpre", "S", "ld")
+
+
+def generator_oracle(case):
+    """A and the gradients of sum(G * A) from oracle.generator (float64)."""
+    import torch
+
+    from oracle import generator as ogen
+
+    g = lambda name: GEN[f"{case}_{name}"]  # noqa: E731
+    vec = bool(g("meta")[1])
+    ins = {k: torch.tensor(g(k), dtype=torch.float64, requires_grad=True) for k in GEN_INPUTS
+           if f"{case}_{k}" in GEN}
+    A = ogen.generator(**ins, ranges=tuple(g("ranges")), vec_dt=vec)
+    A.backward(torch.tensor(g("G"), dtype=torch.float64))
+    return A.detach().numpy(), {k: v.grad.numpy() for k, v in ins.items()}
+
+
+@pytest.mark.parametrize("case", GEN_CASES)
+def test_oracle_generator_matches_reference(case):
+    A, grads = generator_oracle(case)
+    ref = GEN[f"{case}_A"]
+    assert np.abs(A - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max()), str(GEN[f"{case}_type"])
+    for k, got in grads.items():
+        want = GEN[f"{case}_d{k}"]
+        assert np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(want).max()), (str(GEN[f"{case}_type"]), k)
