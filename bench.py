@@ -757,6 +757,34 @@ def time_stream_mix(device, B, N, D, dtype, proj, steps, warmup):
     return time_launches(device, [fwd, bwd], steps, warmup)
 
 
+def time_generator(device, T, n, steps, warmup):
+    """CGHC's generator (conservative + PSD dissipation, the reference's
+    default type, scalar dt) forward + backward over T tokens: the kernel pair,
+    and for context the same steps as eager torch ops on the GPU."""
+    from hyperconnections_b200.ops import cghc_generator
+
+    g = torch.Generator().manual_seed(0)
+    M, R, G = (torch.randn(T, n, n, generator=g).to(device) for _ in range(3))
+    lc, ld = (torch.randn(T, 1, generator=g).to(device) for _ in range(2))
+
+    def kernels():
+        ins = [t.detach().requires_grad_(True) for t in (M, lc, R, ld)]
+        A = cghc_generator(M=ins[0], logit_conserv=ins[1], R=ins[2], logit_diss=ins[3])
+        torch.autograd.grad(A, ins, G)
+
+    def eager():
+        ins = [t.detach().requires_grad_(True) for t in (M, lc, R, ld)]
+        dt_c = 0.001 + 0.999 * torch.sigmoid(ins[1])
+        dt_d = 0.001 + 0.999 * torch.sigmoid(ins[3])
+        A = dt_c.unsqueeze(-1) * (ins[0] - ins[0].transpose(-1, -2))
+        A = A - dt_d.unsqueeze(-1) * (ins[2] @ ins[2].transpose(-1, -2) / n ** 0.5)
+        torch.autograd.grad(A, ins, G)
+
+    k_ms, e_ms = time_launches(device, [kernels, eager], steps, warmup)
+    return {"sweep": "cghc_generator", "tokens": T, "n": n, "type": "conservative_psd_diss", "kernels_ms": k_ms,
+            "torch_eager_gpu_ms": e_ms}
+
+
 SWEEP_N = (2, 3, 4, 6, 8)
 SWEEP_D = (512, 1024, 2048, 4096)
 
@@ -813,6 +841,8 @@ def run_sweep(args):
     for n in (2, 4, 8):
         line = time_sinkhorn(device, TOKENS, n, 20, steps, args.warmup)
         print(json.dumps(line), flush=True)
+    for n in (4, 8):
+        print(json.dumps(time_generator(device, TOKENS, n, steps, args.warmup)), flush=True)
     for n in SWEEP_N:
         ms = float(np.mean(time_expm(device, steps, args.warmup, B=TOKENS, n=n)))
         print(json.dumps({"sweep": "expm_t18", "batch": TOKENS, "n": n, "ms_per_step": ms,
