@@ -759,18 +759,33 @@ def time_stream_mix(device, B, N, D, dtype, proj, steps, warmup):
 
 def time_generator(device, T, n, steps, warmup):
     """CGHC's generator (conservative + PSD dissipation, the reference's
-    default type, scalar dt) forward + backward over T tokens: the kernel pair,
-    and for context the same steps as eager torch ops on the GPU."""
+    default type, scalar dt) forward + backward over T tokens: the kernel pair
+    through the C-ABI, the same through the public API with autograd (host
+    cost included), and for context the same steps as eager torch ops."""
     from hyperconnections_b200.ops import cghc_generator
 
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
     g = torch.Generator().manual_seed(0)
     M, R, G = (torch.randn(T, n, n, generator=g).to(device) for _ in range(3))
     lc, ld = (torch.randn(T, 1, generator=g).to(device) for _ in range(2))
+    A, dM, dR = (torch.empty_like(M) for _ in range(3))
+    dlc, dld = torch.empty_like(lc), torch.empty_like(ld)
+    st = torch.cuda.current_stream(device).cuda_stream
+    ranges = (0.001, 1.0, 0.001, 1.0)
 
-    def kernels():
+    def kernels():  # the C-ABI pair: forward, then backward
+        _lib.check(lib.hc_cghc_generator_fwd(M.data_ptr(), lc.data_ptr(), R.data_ptr(), None, None, ld.data_ptr(),
+                                             A.data_ptr(), T, n, 0, 3, *ranges, st), "hc_cghc_generator_fwd")
+        _lib.check(lib.hc_cghc_generator_bwd(M.data_ptr(), lc.data_ptr(), R.data_ptr(), None, None, ld.data_ptr(),
+                                             G.data_ptr(), dM.data_ptr(), dlc.data_ptr(), dR.data_ptr(), None, None,
+                                             dld.data_ptr(), T, n, 0, 3, *ranges, st), "hc_cghc_generator_bwd")
+
+    def api():
         ins = [t.detach().requires_grad_(True) for t in (M, lc, R, ld)]
-        A = cghc_generator(M=ins[0], logit_conserv=ins[1], R=ins[2], logit_diss=ins[3])
-        torch.autograd.grad(A, ins, G)
+        out = cghc_generator(M=ins[0], logit_conserv=ins[1], R=ins[2], logit_diss=ins[3])
+        torch.autograd.grad(out, ins, G)
 
     def eager():
         ins = [t.detach().requires_grad_(True) for t in (M, lc, R, ld)]
@@ -780,9 +795,9 @@ def time_generator(device, T, n, steps, warmup):
         A = A - dt_d.unsqueeze(-1) * (ins[2] @ ins[2].transpose(-1, -2) / n ** 0.5)
         torch.autograd.grad(A, ins, G)
 
-    k_ms, e_ms = time_launches(device, [kernels, eager], steps, warmup)
+    k_ms, a_ms, e_ms = time_launches(device, [kernels, api, eager], steps, warmup)
     return {"sweep": "cghc_generator", "tokens": T, "n": n, "type": "conservative_psd_diss", "kernels_ms": k_ms,
-            "torch_eager_gpu_ms": e_ms}
+            "api_autograd_ms": a_ms, "torch_eager_gpu_ms": e_ms}
 
 
 SWEEP_N = (2, 3, 4, 6, 8)
