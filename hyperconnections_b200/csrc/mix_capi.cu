@@ -90,8 +90,9 @@ int run_bwd_tma(int sdt, bool fused, bool proj, bool pf32, int n, const WarpGeom
 
 // The pipelined kernels need D % (16 B / element) == 0 (bulk copies move
 // multiples of 16 bytes) and 16-byte aligned stream bases.
-bool use_tma(bool vec, WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int sdt) {
-  return vec && warp_geometry(geo, bwd, fused, n, T, D, dtype_size(sdt), sm_count());
+bool use_tma(bool vec, WarpGeometry& geo, bool bwd, bool fused, bool proj, int n, int64_t T, int64_t D,
+             int sdt) {
+  return vec && warp_geometry(geo, bwd, fused, proj, n, T, D, dtype_size(sdt), sm_count());
 }
 
 }  // namespace
@@ -124,7 +125,7 @@ extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, 
   a.x = x; a.src = Y; a.phi = Phi; a.v = v; a.out = out;
   a.T = B; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
   WarpGeometry geo;
-  if (use_tma(vec, geo, false, false, n, B, D, stream_dtype))
+  if (use_tma(vec, geo, false, false, v != nullptr, n, B, D, stream_dtype))
     return run_fwd_tma(stream_dtype, false, v != nullptr, param_dtype == HC_DTYPE_F32, n, geo, a,
                        static_cast<cudaStream_t>(stream));
   return run_fwd(stream_dtype, false, v != nullptr, vec, param_dtype == HC_DTYPE_F32, n, g, a,
@@ -160,7 +161,7 @@ extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, 
   a.grad_x = D > 0 ? grad_x : nullptr; a.grad_phi = grad_Phi; a.grad_v = grad_v;
   a.T = B; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
   WarpGeometry geo;
-  if (use_tma(vec, geo, true, false, n, B, D, stream_dtype))
+  if (use_tma(vec, geo, true, false, v != nullptr, n, B, D, stream_dtype))
     return run_bwd_tma(stream_dtype, false, v != nullptr, param_dtype == HC_DTYPE_F32, n, geo, a,
                        static_cast<cudaStream_t>(stream));
   // D == 0 still writes the (all-zero) parameter gradients.
@@ -184,7 +185,7 @@ extern "C" int hc_fused_fwd(const void* x, const void* f, const float* H, const 
   a.x = x; a.src = f; a.phi = H; a.alpha = alpha; a.beta = beta; a.out = x_out; a.u = u;
   a.T = T; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
   WarpGeometry geo;
-  if (use_tma(vec, geo, false, true, n, T, D, stream_dtype))
+  if (use_tma(vec, geo, false, true, false, n, T, D, stream_dtype))
     return run_fwd_tma(stream_dtype, true, false, true, n, geo, a, static_cast<cudaStream_t>(stream));
   return run_fwd(stream_dtype, true, false, vec, true, n, g, a, static_cast<cudaStream_t>(stream));
 }
@@ -213,7 +214,7 @@ extern "C" int hc_fused_bwd(const void* g_u, const void* g_x, const void* x, con
   a.grad_phi = grad_H; a.grad_alpha = grad_alpha; a.grad_beta = grad_beta;
   a.T = T; a.D = D; a.nchunk = g.nchunk; a.passes = g.passes;
   WarpGeometry geo;
-  if (use_tma(vec, geo, true, true, n, T, D, stream_dtype))
+  if (use_tma(vec, geo, true, true, false, n, T, D, stream_dtype))
     return run_bwd_tma(stream_dtype, true, false, true, n, geo, a, static_cast<cudaStream_t>(stream));
   return run_bwd(stream_dtype, true, false, vec, true, n, g, a, static_cast<cudaStream_t>(stream));
 }
@@ -228,9 +229,15 @@ extern "C" int hc_wait_timeouts(unsigned int* count, int reset) {
   return HC_OK;
 }
 
+// HC_PRODUCER_LANES (build flag, 0 = automatic) fixes the producer lanes of
+// every ring, for measurements.
+#ifndef HC_PRODUCER_LANES
+#define HC_PRODUCER_LANES 0
+#endif
+
 namespace hc {
 WarpTuning& warp_tuning() {
-  static WarpTuning t{0, 0, 0};
+  static WarpTuning t{0, 0, 0, HC_PRODUCER_LANES};
   return t;
 }
 }  // namespace hc
@@ -238,6 +245,6 @@ WarpTuning& warp_tuning() {
 extern "C" int hc_set_mix_tuning(int stage_bytes, int stages, int warps) {
   if (stage_bytes < 0 || stages < 0 || stages > kRingMaxStages || warps < 0 || warps >= kWarpMaxWarps)
     return HC_ERR_BAD_SIZE;
-  hc::warp_tuning() = hc::WarpTuning{stage_bytes, stages, warps};
+  hc::warp_tuning() = hc::WarpTuning{stage_bytes, stages, warps, hc::warp_tuning().producers};
   return HC_OK;
 }

@@ -2,8 +2,9 @@
 //
 // A persistent CTA per SM owns a contiguous range of tokens and a ring of
 // shared-memory stages, each with a "full" and an "empty" mbarrier. Warp 0 is
-// the producer: one lane issues the bulk copies (plain cp.async.bulk into this CTA only)
-// of the next token (or token-slice) into the next free stage with
+// the producer: one lane (four, in lockstep, for rings of small or sliced
+// items) issues the bulk copies (plain cp.async.bulk into this CTA only) of
+// the next token (or token-slice) into the next free stage with
 // arrive.expect_tx on its full barrier. Warps 1..C are consumers: consumer c
 // takes tokens c, c + C, ... of the range, waits on the stage's full barrier,
 // computes in fp32 registers, stores 8-byte coalesced words to global memory,
@@ -24,7 +25,8 @@
 // stores). A token stays on one consumer warp, so the backward's per-token
 // sums (grad_Phi / grad_H, grad_alpha, grad_beta, the projection terms)
 // accumulate in registers over all slices and fold with one warp
-// transpose-reduce.
+// transpose-reduce; at n >= 5 with sliced tokens the sums go to a per-warp
+// Gram in shared memory a block of rows at a time (the blocked backward).
 //
 // Every wait is bounded (kWaitLimit polls). A warp that gives up counts it in
 // a device counter (hc_wait_timeouts) and raises the CTA's abort flag; all
@@ -169,14 +171,19 @@ struct WarpGeometry {
   int stage_bytes;  // rows * pitch * element size
   int grid;         // CTAs
   int smem_bytes;   // dynamic shared memory per CTA
+  int producers;    // lanes of warp 0 that issue fills (1 <= producers <= stages)
 };
+
 
 // Warps per CTA at most (producer included). The forward keeps 16 warps (128
 // registers per thread) for n <= 4; the packed-pair backward for n <= 4 needs
-// up to 170 registers, so 12 warps; larger n use 8 warps (255 registers).
+// up to 170 registers, so 12 warps, and so does the blocked backward (tokens
+// cut into slices at n >= 5); the backward of whole tokens at n = 7, 8 keeps
+// all its sums in registers and runs 8 warps (255 registers).
 constexpr int fwd_warp_cap(int n) { return n <= 4 ? 16 : 8; }
-constexpr int bwd_warp_cap(int n) { return n <= 6 ? 12 : 8; }
-constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap(n) : fwd_warp_cap(n); }
+constexpr int bwd_warp_cap(int n, bool blocked) { return blocked || n <= 6 ? 12 : 8; }
+constexpr int bwd_warp_cap_max() { return 12; }
+constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap_max() : fwd_warp_cap(n); }
 
 // Issue the bulk copies of one item (cnt consecutive tokens, or one slice of
 // one token) into a stage. Stage layout: [tensor][token][row][pitch].
@@ -235,48 +242,115 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
   __syncthreads();
 }
 
-// Producer loop (one lane). Work is cut into "units" (tpi consecutive tokens)
-// dealt round-robin to the C consumers; units are issued in groups of C,
-// slice-major inside a group, so consecutive items of one consumer are at most
-// C apart and every consumer has its next item in flight. Item k goes to stage
-// k mod S; the producer reuses a stage once the consumer of item k - S has
-// released it.
+// Position of one item in the producer's sequence: unit group g0, slice p,
+// unit w inside the group (Wg units in it), stage s with its fill parity ph,
+// item index k.
+struct ProducerCursor {
+  int g0, p, w, Wg, s;
+  uint32_t ph;
+  int64_t k;
+  __device__ __forceinline__ void step(int C, int ns, int nunits, int S) {
+    if (++w == Wg) {
+      w = 0;
+      if (++p == ns) {
+        p = 0;
+        g0 += C;
+        Wg = min(C, nunits - g0);
+      }
+    }
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    ++k;
+  }
+};
+
+// Producer loop, run by lanes 0 .. P - 1 of warp 0 (P = geo.producers).
+// Work is cut into "units" (tpi consecutive tokens) dealt round-robin to the
+// C consumers; units are issued in groups of C, slice-major inside a group, so
+// consecutive items of one consumer are at most C apart and every consumer has
+// its next item in flight. Item k goes to stage k mod S; a stage is reused
+// once the consumer of item k - S has released it.
+//
+// One issuing thread fills a stage every ~250 ns whatever the copy size (a
+// fixed cost per fill, measured on B200 with consumers that release at once),
+// which caps 8 KB items near 4 TB/s. With P > 1, lane q issues items k = q,
+// q + P, q + 2P, ...: the P lanes fill P consecutive items per round in
+// lockstep. Within a round the P items sit in distinct stages (P <= S) and
+// wait only on releases of items of earlier rounds, all issued, and every
+// lane has seen the release of item k - 2S before it waits on the release of
+// item k - S, so a parity wait can never mistake an older phase for the one
+// it waits on.
 template <typename T, int NIN>
 __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& geo, uint8_t* smem, int64_t D,
                                              int64_t t_begin, int ntok, int nunits, const void* const* base,
-                                             const int* rows) {
-  const int S = geo.stages, C = geo.consumers;
-  int s = 0;
-  uint32_t ph = 0;
-  int64_t k = 0;
-  for (int g0 = 0; g0 < nunits; g0 += C) {
-    const int Wg = min(C, nunits - g0);
-    for (int p = 0; p < geo.ns; ++p) {
-      for (int w = 0; w < Wg; ++w) {
-        if (st.abort) return;
-        if (k >= S) {
-          if (!warp_wait(&st.empty[s], ph ^ 1u)) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
-            st.abort = 1;
-            return;
+                                             const int* rows, int lane) {
+  const int S = geo.stages, C = geo.consumers, P = geo.producers;
+  if (P == 1) {
+    int s = 0;
+    uint32_t ph = 0;
+    int64_t k = 0;
+    for (int g0 = 0; g0 < nunits; g0 += C) {
+      const int Wg = min(C, nunits - g0);
+      for (int p = 0; p < geo.ns; ++p) {
+        for (int w = 0; w < Wg; ++w) {
+          if (st.abort) return;
+          if (k >= S) {
+            if (!warp_wait(&st.empty[s], ph ^ 1u)) {
+              atomicAdd(&g_mix_wait_timeouts, 1u);
+              st.abort = 1;
+              return;
+            }
+            fence_proxy_async_smem();
           }
-          fence_proxy_async_smem();
-        }
-        const int u = g0 + w;
-        const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
-                           t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
-        __threadfence_block();  // the arrive.expect_tx above is visible before the tag
-        st.tag[s] = k;
-        st.issued[s] = 1;
-        st.last_parity[s] = ph;
-        ++k;
-        if (++s == S) {
-          s = 0;
-          ph ^= 1u;
+          const int u = g0 + w;
+          const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+          ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
+                             t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
+          __threadfence_block();  // the arrive.expect_tx above is visible before the tag
+          st.tag[s] = k;
+          st.issued[s] = 1;
+          st.last_parity[s] = ph;
+          ++k;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
       }
     }
+    return;
+  }
+  const unsigned mask = P >= 32 ? kFull : (1u << P) - 1u;
+  ProducerCursor c{0, 0, 0, min(C, nunits), 0, 0u, 0};
+  for (int i = 0; i < lane; ++i) c.step(C, geo.ns, nunits, S);
+  while (true) {
+    const bool act = c.g0 < nunits;
+    if (!__any_sync(mask, act)) break;
+    bool fail = false;
+    if (act && !st.abort) {
+      if (c.k >= S) {
+        fail = !warp_wait(&st.empty[c.s], c.ph ^ 1u);
+        if (!fail) fence_proxy_async_smem();
+      }
+      if (!fail) {
+        const int u = c.g0 + c.w;
+        const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(c.s) * geo.stage_bytes, &st.full[c.s],
+                           t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, c.p, base, rows);
+        st.issued[c.s] = 1;
+        st.last_parity[c.s] = c.ph;
+        __threadfence_block();  // expect_tx and the drain record are visible before the tag
+        st.tag[c.s] = c.k;
+      }
+    }
+    if (fail) {
+      atomicAdd(&g_mix_wait_timeouts, 1u);
+      st.abort = 1;
+    }
+    if (__any_sync(mask, st.abort)) break;
+    for (int i = 0; i < P; ++i) c.step(C, geo.ns, nunits, S);
   }
 }
 
@@ -669,10 +743,10 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   const bool single = geo.tpi == 1;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane < geo.producers) {
       const void* base[2] = {a.x, a.src};
       const int rows[2] = {N, NS};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
+      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -889,14 +963,201 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const Params& pr
   }
 }
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
-__global__ void __launch_bounds__(bwd_warp_cap(N) * 32, 1)
+// ------------------------------------------- blocked backward for n >= 5
+// With n >= 5 the per-lane sums of the backward (n^2 + 2n of them) and Phi
+// together no longer leave room for 12 warps. The blocked path splits each
+// slice's work instead:
+//   pass A  grad_x (and grad_f) of the slice, no sums;
+//   pass B  the slice's Gram sums, a block of rows at a time: a block fills
+//           at most 32 sums per lane, one warp transpose-reduce leaves one sum
+//           per lane, and that lane adds it into the warp's Gram in shared
+//           memory;
+//   finish  at the token's last slice, the parameter gradients from the Gram.
+// The Gram is M = A B^T over the slice's elements, with A's rows g_0..g_{n-1}
+// and B's rows x_0..x_{n-1}, each extended by g_u and f in the fused step.
+// Then grad_Phi_ij = M_ij, and in the fused step grad_alpha_j = M_nj and
+// grad_beta_i = M_in.
+// The blocked path runs at n >= 5 for tokens cut into slices, without the
+// projection. Measured on B200: +1-7% there; the single pass with every sum
+// in registers is faster for whole tokens (by 16% at n = 8, D = 512) and with
+// the projection (by 11-15%, sliced or not).
+constexpr bool bwd_blocked_n(int n, bool proj) { return n >= 5 && !proj; }
+inline bool bwd_blocked(int n, bool proj, int ns) { return bwd_blocked_n(n, proj) && ns > 1; }
+
+template <int N, bool FUSED>
+struct GramShape {
+  static constexpr bool EXTRA = FUSED;
+  static constexpr int NA = N + (EXTRA ? 1 : 0);  // rows (and columns) of M
+  static constexpr int SIZE = NA * NA;
+  static constexpr int RB = 32 / NA;              // rows per block: RB * NA <= 32 sums
+};
+
+// Pass A: grad_x_j = sum_i Phi_ij g_i (+ alpha_j g_u) and grad_f = beta^T g
+// over one slice; same arithmetic as bwd_slice.
+template <typename T, typename P, int N, bool FUSED, int W>
+__device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, false>& pr,
+                                                const uint8_t* gsb, const uint8_t* usb, int pitch, int64_t t,
+                                                int64_t d0, int len, int lane) {
+  using Wd = Word<T>;
+  constexpr int K = Wd::K;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
+  T* gft = (FUSED && a.grad_f) ? static_cast<T*>(a.grad_f) + t * D + d0 : nullptr;
+  if (gxt == nullptr && gft == nullptr) return;
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
+    Words<W> gw_[N], uw;
+#pragma unroll
+    for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(gsb + eo + r * rowb);
+    if constexpr (FUSED) uw = lds_words<W>(usb + eo);
+    uint32_t gxo[N][W], gfo[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float ge[N][K], gue[K];
+#pragma unroll
+      for (int r = 0; r < N; ++r) Wd::get(gw_[r].w[w], ge[r]);
+      if constexpr (FUSED) Wd::get(uw.w[w], gue);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float s = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) s = fmaf(pr.phi[i2 * N + j], ge[i2][e], s);
+          if constexpr (FUSED) s = fmaf(pr.al[j], gue[e], s);
+          o[e] = s;
+        }
+        gxo[j][w] = Wd::put(o);
+      }
+      if constexpr (FUSED) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float s = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) s = fmaf(pr.be[i2], ge[i2][e], s);
+          o[e] = s;
+        }
+        gfo[w] = Wd::put(o);
+      }
+    }
+    if (gxt) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) stg_words<W>(gxt + j * D + e0, gxo[j]);
+    }
+    if constexpr (FUSED) {
+      if (gft) stg_words<W>(gft + e0, gfo);
+    }
+  }
+}
+
+// Pass B for the rows [R0, R0 + RB) of M over one slice, added into the
+// warp's Gram (row-major, NA x NA, in shared memory). Lane l owns entry
+// R0 * NA + l of the block, in every slice, so its read-modify-write needs no
+// synchronisation.
+template <typename T, int N, bool FUSED, int W, int R0>
+__device__ __forceinline__ void bwd_gram_block(float* gram, const uint8_t* gsb, const uint8_t* xsb,
+                                               const uint8_t* usb, const uint8_t* fsb, int pitch, int len,
+                                               int lane) {
+  using G = GramShape<N, FUSED>;
+  using Wd = Word<T>;
+  constexpr int K = Wd::K;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  constexpr int NA = G::NA;
+  constexpr int RB = G::RB < NA - R0 ? G::RB : NA - R0;
+  constexpr bool HAS_EXTRA = G::EXTRA && R0 + RB > N;  // the block ends with row n of M (g_u)
+  constexpr int RG = HAS_EXTRA ? RB - 1 : RB;          // g rows of the block
+  constexpr int NGW = RG > 0 ? RG : 1;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  float acc[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
+    Words<W> xw[N], fw, gw[NGW], uw;
+#pragma unroll
+    for (int j = 0; j < N; ++j) xw[j] = lds_words<W>(xsb + eo + j * rowb);
+    if constexpr (FUSED) fw = lds_words<W>(fsb + eo);
+#pragma unroll
+    for (int r = 0; r < RG; ++r) gw[r] = lds_words<W>(gsb + eo + (R0 + r) * rowb);
+    if constexpr (HAS_EXTRA) uw = lds_words<W>(usb + eo);
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float col[NA][K], row[RB][K];
+#pragma unroll
+      for (int j = 0; j < N; ++j) Wd::get(xw[j].w[w], col[j]);
+      if constexpr (FUSED) Wd::get(fw.w[w], col[N]);
+#pragma unroll
+      for (int r = 0; r < RG; ++r) Wd::get(gw[r].w[w], row[r]);
+      if constexpr (HAS_EXTRA) Wd::get(uw.w[w], row[RG]);
+#pragma unroll
+      for (int e = 0; e < K; ++e) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+#pragma unroll
+          for (int j = 0; j < NA; ++j) {
+            if (R0 + r == N && j == N) continue;  // M_nn is not used
+            acc[r * NA + j] = fmaf(row[r][e], col[j][e], acc[r * NA + j]);
+          }
+        }
+      }
+    }
+  }
+  warp_transpose_reduce<1>(acc, lane);  // lane l: the warp's sum of entry l
+  if (lane < RB * NA) gram[R0 * NA + lane] += acc[0];
+}
+
+template <typename T, int N, bool FUSED, int W, int R0>
+__device__ __forceinline__ void bwd_gram_slice(float* gram, const uint8_t* gsb, const uint8_t* xsb,
+                                               const uint8_t* usb, const uint8_t* fsb, int pitch, int len,
+                                               int lane) {
+  using G = GramShape<N, FUSED>;
+  if constexpr (R0 < G::NA) {
+    bwd_gram_block<T, N, FUSED, W, R0>(gram, gsb, xsb, usb, fsb, pitch, len, lane);
+    bwd_gram_slice<T, N, FUSED, W, R0 + G::RB>(gram, gsb, xsb, usb, fsb, pitch, len, lane);
+  }
+}
+
+// The token's parameter gradients from its Gram, then the Gram cleared for
+// the warp's next token.
+template <int N, bool FUSED>
+__device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, float* gram, int64_t t, int lane) {
+  using G = GramShape<N, FUSED>;
+  constexpr int NA = G::NA;
+  __syncwarp();
+  if (a.grad_phi) {
+#pragma unroll
+    for (int q = 0; q < (N * N + 31) / 32; ++q) {
+      const int k = lane + 32 * q;
+      if (k < N * N) a.grad_phi[t * (N * N) + k] = gram[(k / N) * NA + k % N];
+    }
+  }
+  if constexpr (FUSED) {
+    if (lane < N) {
+      if (a.grad_alpha) a.grad_alpha[t * N + lane] = gram[N * NA + lane];
+      if (a.grad_beta) a.grad_beta[t * N + lane] = gram[lane * NA + N];
+    }
+  }
+  __syncwarp();
+  for (int k = lane; k < G::SIZE; k += 32) gram[k] = 0.f;
+  __syncwarp();
+}
+
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK>
+__global__ void __launch_bounds__(bwd_warp_cap(N, BLK) * 32, 1)
 mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
   constexpr int es = sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
+  // per-consumer Gram of the blocked path
+  __shared__ float gram_all[BLK ? (kWarpMaxWarps - 1) * GramShape<N, FUSED>::SIZE : 1];
   ring_init(st, geo.stages);
 
   const int64_t T_ = a.T, D = a.D;
@@ -911,7 +1172,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   const bool single = geo.tpi == 1;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane < geo.producers) {
       const void* base[NIN];
       int rows[NIN];
       base[0] = a.g;
@@ -924,15 +1185,22 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         rows[2] = 1;
         rows[3] = 1;
       }
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
     constexpr bool PAIRS = use_pairs(N);
+    constexpr bool BLOCKED = BLK;
     using Params = std::conditional_t<PAIRS, TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
     Params pr;
-    float acc[L::kPad];
+    float acc[BLOCKED ? 1 : L::kPad];
     float2 acc2[PAIRS ? L::kAcc : 1];
+    float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
+    if constexpr (BLOCKED) {
+      static_assert(!PROJ, "the blocked path has no projection terms");
+      for (int k = lane; k < GramShape<N, FUSED>::SIZE; k += 32) gram[k] = 0.f;
+      __syncwarp();
+    }
     RingCursor cur{c, 0u, c};
     for (int g0 = 0; g0 < nunits; g0 += C) {
       const int Wg = min(C, nunits - g0);
@@ -957,8 +1225,10 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         auto token = [&](int tt, int64_t t) {
           if (p == 0) {
             if (tt > 0) pr.load(a.phi, a.v, a.alpha, a.beta, t);
+            if constexpr (!BLOCKED) {
 #pragma unroll
-            for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+              for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+            }
             if constexpr (PAIRS) {
 #pragma unroll
               for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
@@ -968,17 +1238,23 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
           const uint8_t* xs = sb + nreg + tt * N * rowb;
           const uint8_t* us = sb + 2 * nreg + tt * rowb;
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
-          if constexpr (PAIRS) {
-            bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
+          if constexpr (BLOCKED) {
+            bwd_grads_slice<T, P, N, FUSED, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
+            bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
+            if (p == ns - 1) bwd_gram_finish<N, FUSED>(a, gram, t, lane);
           } else {
-            bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
-          }
-          if (p == ns - 1) {  // token complete (tpi > 1 only with ns == 1)
             if constexpr (PAIRS) {
-#pragma unroll
-              for (int k = 0; k < L::kAcc; ++k) acc[k] = acc2[k].x + acc2[k].y;
+              bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
+            } else {
+              bwd_slice<T, P, N, FUSED, PROJ, W>(a, pr, acc, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
             }
-            bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
+            if (p == ns - 1) {  // token complete (tpi > 1 only with ns == 1)
+              if constexpr (PAIRS) {
+#pragma unroll
+                for (int k = 0; k < L::kAcc; ++k) acc[k] = acc2[k].x + acc2[k].y;
+              }
+              bwd_finish<P, N, FUSED, PROJ>(a, pr, acc, t, lane);
+            }
           }
         };
         if (single) {
@@ -1007,6 +1283,7 @@ struct WarpTuning {
   int stage_bytes;  // target bytes of an item of several small tokens
   int stages;       // stages of the ring
   int warps;        // consumer warps per CTA
+  int producers;    // producer lanes (not part of the C ABI; fixed by a build flag)
 };
 WarpTuning& warp_tuning();
 
@@ -1046,6 +1323,7 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   if (consumers < 1 || stages < 3) return false;
   geo.stages = stages;
   geo.consumers = consumers;
+  geo.producers = 1;
   geo.smem_bytes = stages * geo.stage_bytes;
   geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
   return true;
@@ -1064,10 +1342,30 @@ inline void prefer_bwd_consumers(WarpGeometry& geo, int n) {
   }
 }
 
-inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, int n, int64_t T, int64_t D, int esize,
-                          int num_sms) {
+// Four producer lanes where a fill is small or made of many row copies (a
+// token cut into slices, one copy per row slice): measured on B200, +6-19%
+// for such backward rings and +12% for the mix-write forward, while rings of
+// whole tokens of 12 KB or more (the fused forward and backward at n = 4,
+// D = 768 among them) lose 1-3% to the lockstep rounds.
+constexpr int kSmallFillBytes = 12 * 1024;
+constexpr int kManyFillLanes = 4;
+inline void prefer_producers(WarpGeometry& geo) {
+  if (warp_tuning().producers > 0) {
+    geo.producers = std::min(warp_tuning().producers, geo.stages);
+  } else if (geo.ns > 1 || geo.stage_bytes < kSmallFillBytes) {
+    geo.producers = std::min(kManyFillLanes, geo.stages);
+  }
+}
+
+inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, int n, int64_t T, int64_t D,
+                          int esize, int num_sms) {
   if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
-  if (bwd && warp_cap(bwd, n) > 8) prefer_bwd_consumers(geo, n);
+  if (bwd) {
+    const int cap = bwd_warp_cap(n, bwd_blocked(n, proj, geo.ns));
+    geo.consumers = std::min(geo.consumers, cap - 1);
+    if (cap > 8) prefer_bwd_consumers(geo, n);
+    prefer_producers(geo);
+  }
   return true;
 }
 
@@ -1082,7 +1380,7 @@ inline int warp_prepare(KernelT* kernel, int smem_bytes) {
 // 8-byte accesses elsewhere; 4-byte accesses for the backward at n = 5, 6,
 // which then fits 12 warps without spilling (register budget).
 constexpr int fwd_lane_words(int n) { return n <= 4 ? 4 : 2; }
-constexpr int bwd_lane_words(int n) { return (n == 5 || n == 6) ? 1 : 2; }
+constexpr int bwd_lane_words(int n, bool blocked) { return blocked || n == 5 || n == 6 ? 1 : 2; }
 
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cudaStream_t s) {
@@ -1102,15 +1400,29 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cud
   return launch_status();
 }
 
+template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK>
+int launch_bwd_kernel(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
+  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK>;
+  if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
+  k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);
+  return HC_OK;
+}
+
+template <typename T, typename P, int N, bool FUSED, bool PROJ>
+int launch_bwd_one(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
+  if constexpr (bwd_blocked_n(N, PROJ)) {
+    if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+  }
+  return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, block, a, s);
+}
+
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_bwd_warp(int n, const WarpGeometry& geo, const MixBwdArgs& a, cudaStream_t s) {
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
-    auto* k = mix_bwd_warp_kernel<T, P, NN, FUSED, PROJ, bwd_lane_words(NN)>; \
-    if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;            \
-    k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);                  \
+    if (int rc = launch_bwd_one<T, P, NN, FUSED, PROJ>(geo, block, a, s)) return rc; \
     break;                                                              \
   }
     HC_CASE(1) HC_CASE(2) HC_CASE(3) HC_CASE(4) HC_CASE(5) HC_CASE(6) HC_CASE(7) HC_CASE(8)

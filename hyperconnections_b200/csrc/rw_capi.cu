@@ -42,6 +42,7 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
   const int cap = rw_cap(bwd, n, m, mixw, proj);
   if (!ring_geometry(geo, rw_rows(bwd, n, m, mixw), cap, T, D, es, sm_count(), bwd)) return false;
   if (bwd && cap > 8) prefer_bwd_consumers(geo, 4);  // the read / mix-write caps exceed 8 only for small tokens
+  if (mixw) prefer_producers(geo);
   return true;
 }
 

@@ -174,10 +174,10 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   const uint32_t xregion = static_cast<uint32_t>(geo.tpi) * N * rowb;  // x rows of all tokens of a stage
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane < geo.producers) {
       const void* base[2] = {a.x, a.f};
       const int rows[2] = {N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -422,10 +422,10 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   const uint32_t xreg = static_cast<uint32_t>(geo.tpi) * N * rowb;   // x rows of all tokens of a stage
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane < geo.producers) {
       const void* base[3] = {a.g, a.x, a.f};
       const int rows[3] = {NG, N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
