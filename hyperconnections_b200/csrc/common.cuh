@@ -246,4 +246,8 @@ inline int dtype_size(int dt) {
   }
 }
 
+// Bounded waits of the expm kernels that gave up (expm.cu); summed into
+// hc_wait_timeouts() with those of the ring kernels.
+unsigned int expm_take_timeouts(bool reset);
+
 }  // namespace hc

@@ -33,6 +33,7 @@
 // of the Matrix Exponential, with an Application to Condition Number
 // Estimation", SIAM J. Matrix Anal. Appl. 30 (2009)). The scaling exponent is
 // the forward's (from ||A||_1, not ||A^T||_1).
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -531,6 +532,441 @@ __global__ void __launch_bounds__(kExpmThreads) expm_t18_bwd_kernel(const float*
   store_row<N>(dA, mat, batch, r, dt);
 }
 
+// ------------------------------------------------ one thread per matrix (n <= 4)
+// For n <= 4 a whole matrix (at most 16 floats) fits one thread's registers,
+// and a product is n^3 FMAs with no shuffle at all. These helpers perform the
+// operations of the row-per-lane scheme above element for element, in the
+// same order (products accumulate over k ascending from 0; the column sums of
+// ||A||_1 add rows pairwise as the xor-shuffle tree does; the identity term
+// is added as `s + c0` or `s + 0`), so the forward below returns bitwise the
+// results of expm_t18_fwd_kernel.
+template <int N>
+__device__ __forceinline__ void tm_mm(const float (&a)[N][N], const float (&b)[N][N], float (&c)[N][N]) {
+  float o[N][N];
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) o[i][j] = 0.f;
+#pragma unroll
+  for (int k = 0; k < N; ++k)
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) o[i][j] = fmaf(a[i][k], b[k][j], o[i][j]);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) c[i][j] = o[i][j];
+}
+
+template <int N>
+__device__ __forceinline__ void tm_combo(float (&o)[N][N], float c0, float c1, const float (&x1)[N][N], float c2,
+                                         const float (&x2)[N][N], float c3, const float (&x3)[N][N], float c6,
+                                         const float (&x6)[N][N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float s = c1 * x1[i][j];
+      s = fmaf(c2, x2[i][j], s);
+      s = fmaf(c3, x3[i][j], s);
+      s = fmaf(c6, x6[i][j], s);
+      o[i][j] = s + (j == i ? c0 : 0.f);
+    }
+}
+
+// T18 from the powers a, a2 = a a, a3 = a2 a, a6 = a3 a3 (the combinations
+// and the two remaining products).
+template <int N>
+__device__ __forceinline__ void tm_t18_tail(const float (&a)[N][N], const float (&a2)[N][N],
+                                            const float (&a3)[N][N], const float (&a6)[N][N], float (&t)[N][N]) {
+  const float z[N][N] = {};
+  float b1[N][N], b4[N][N], b5[N][N], a9[N][N];
+  tm_combo<N>(b1, 0.f, kA11, a, kA21, a2, kA31, a3, 0.f, z);
+  tm_combo<N>(b5, 0.f, 0.f, a, kB24, a2, kB34, a3, kB64, a6);
+  tm_combo<N>(b4, kB03, kB13, a, kB23, a2, kB33, a3, kB63, a6);
+  tm_mm<N>(b1, b5, a9);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) a9[i][j] += b4[i][j];
+  float b2[N][N], b3[N][N];
+  tm_combo<N>(b2, 0.f, kB11, a, kB21, a2, kB31, a3, kB61, a6);
+  tm_combo<N>(b3, kB02, kB12, a, kB22, a2, kB32, a3, kB62, a6);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) b3[i][j] += a9[i][j];
+  float p[N][N];
+  tm_mm<N>(b3, a9, p);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) t[i][j] = b2[i][j] + p[i][j];
+}
+
+template <int N>
+__device__ __forceinline__ void tm_powers(const float (&a)[N][N], float (&a2)[N][N], float (&a3)[N][N],
+                                          float (&a6)[N][N]) {
+  tm_mm<N>(a, a, a2);
+  tm_mm<N>(a2, a, a3);
+  tm_mm<N>(a3, a3, a6);
+}
+
+template <int N>
+__device__ __forceinline__ void tm_t18(const float (&a)[N][N], float (&t)[N][N]) {
+  float a2[N][N], a3[N][N], a6[N][N];
+  tm_powers<N>(a, a2, a3, a6);
+  tm_t18_tail<N>(a, a2, a3, a6, t);
+}
+
+template <int N>
+__device__ __forceinline__ void tm_scale(float (&x)[N][N], float c) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[i][j] *= c;
+}
+
+// (C, dC) = (A B, dA B + A dB), the per-element order of mm_d.
+template <int N>
+__device__ __forceinline__ void tm_mm_d(const float (&a)[N][N], const float (&da)[N][N], const float (&b)[N][N],
+                                        const float (&db)[N][N], float (&c)[N][N], float (&dc)[N][N]) {
+  float o[N][N], d[N][N];
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      o[i][j] = 0.f;
+      d[i][j] = 0.f;
+    }
+#pragma unroll
+  for (int k = 0; k < N; ++k)
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        o[i][j] = fmaf(a[i][k], b[k][j], o[i][j]);
+        d[i][j] = fmaf(da[i][k], b[k][j], d[i][j]);
+        d[i][j] = fmaf(a[i][k], db[k][j], d[i][j]);
+      }
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      c[i][j] = o[i][j];
+      dc[i][j] = d[i][j];
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void tm_dcombo(float (&o)[N][N], float c1, const float (&x1)[N][N], float c2,
+                                          const float (&x2)[N][N], float c3, const float (&x3)[N][N], float c6,
+                                          const float (&x6)[N][N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float s = c1 * x1[i][j];
+      s = fmaf(c2, x2[i][j], s);
+      s = fmaf(c3, x3[i][j], s);
+      o[i][j] = fmaf(c6, x6[i][j], s);
+    }
+}
+
+// T18 and its forward-mode derivative in direction da, the steps of
+// t18_eval_d.
+template <int N>
+__device__ __forceinline__ void tm_t18_d(const float (&a)[N][N], const float (&da)[N][N], float (&t)[N][N],
+                                         float (&dt)[N][N]) {
+  float a2[N][N], a3[N][N], a6[N][N], d2[N][N], d3[N][N], d6[N][N];
+  tm_mm_d<N>(a, da, a, da, a2, d2);
+  tm_mm_d<N>(a2, d2, a, da, a3, d3);
+  tm_mm_d<N>(a3, d3, a3, d3, a6, d6);
+  const float z[N][N] = {};
+  float b1[N][N], b5[N][N], db1[N][N], db5[N][N];
+  tm_combo<N>(b1, 0.f, kA11, a, kA21, a2, kA31, a3, 0.f, z);
+  tm_dcombo<N>(db1, kA11, da, kA21, d2, kA31, d3, 0.f, z);
+  tm_combo<N>(b5, 0.f, 0.f, a, kB24, a2, kB34, a3, kB64, a6);
+  tm_dcombo<N>(db5, 0.f, da, kB24, d2, kB34, d3, kB64, d6);
+  float a9[N][N], d9[N][N];
+  tm_mm_d<N>(b1, db1, b5, db5, a9, d9);
+  {
+    float b4[N][N], db4[N][N];
+    tm_combo<N>(b4, kB03, kB13, a, kB23, a2, kB33, a3, kB63, a6);
+    tm_dcombo<N>(db4, kB13, da, kB23, d2, kB33, d3, kB63, d6);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        a9[i][j] += b4[i][j];
+        d9[i][j] += db4[i][j];
+      }
+  }
+  float b2[N][N], b3[N][N], db2[N][N], db3[N][N];
+  tm_combo<N>(b2, 0.f, kB11, a, kB21, a2, kB31, a3, kB61, a6);
+  tm_dcombo<N>(db2, kB11, da, kB21, d2, kB31, d3, kB61, d6);
+  tm_combo<N>(b3, kB02, kB12, a, kB22, a2, kB32, a3, kB62, a6);
+  tm_dcombo<N>(db3, kB12, da, kB22, d2, kB32, d3, kB62, d6);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      b3[i][j] += a9[i][j];
+      db3[i][j] += d9[i][j];
+    }
+  float p[N][N], dp[N][N];
+  tm_mm_d<N>(b3, db3, a9, d9, p, dp);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      t[i][j] = b2[i][j] + p[i][j];
+      dt[i][j] = db2[i][j] + dp[i][j];
+    }
+}
+
+// ||A||_1: column sums of |a_ij| over the rows added pairwise (row 0 + row 1,
+// row 2 + row 3, then the two), the order of the xor-shuffle tree of
+// norm1_rows; a missing fourth row of n = 3 adds an exact zero there too.
+template <int N>
+__device__ __forceinline__ float tm_norm1(const float (&a)[N][N]) {
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    float s;
+    if constexpr (N == 1) {
+      s = fabsf(a[0][j]);
+    } else if constexpr (N == 2) {
+      s = fabsf(a[0][j]) + fabsf(a[1][j]);
+    } else if constexpr (N == 3) {
+      s = (fabsf(a[0][j]) + fabsf(a[1][j])) + (fabsf(a[2][j]) + 0.f);
+    } else {
+      s = (fabsf(a[0][j]) + fabsf(a[1][j])) + (fabsf(a[2][j]) + fabsf(a[3][j]));
+    }
+    m = fmaxf(m, s);
+  }
+  return m;
+}
+
+template <int N>
+__device__ __forceinline__ void tm_load(const float* __restrict__ base, int64_t m, bool vec, float (&a)[N][N]) {
+  const float* p = base + m * (N * N);
+  if constexpr ((N * N) % 4 == 0) {
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < N * N / 4; ++q) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p) + q);
+        const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a[(4 * q + e) / N][(4 * q + e) % N] = w[e];
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) a[i][j] = __ldg(p + i * N + j);
+}
+
+template <int N>
+__device__ __forceinline__ void tm_store(float* __restrict__ base, int64_t m, bool vec, const float (&a)[N][N]) {
+  float* p = base + m * (N * N);
+  if constexpr ((N * N) % 4 == 0) {
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < N * N / 4; ++q) {
+        float4 v;
+        v.x = a[(4 * q) / N][(4 * q) % N];
+        v.y = a[(4 * q + 1) / N][(4 * q + 1) % N];
+        v.z = a[(4 * q + 2) / N][(4 * q + 2) % N];
+        v.w = a[(4 * q + 3) / N][(4 * q + 3) % N];
+        reinterpret_cast<float4*>(p)[q] = v;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[i * N + j] = a[i][j];
+}
+
+// Largest batch exponent for which the first matrix's powers formed before
+// the grid barrier are used (||A||_1 <= 3.01 * 2^10: A^6 stays far from
+// overflow, and A^6 2^-60 from the subnormal range for entries of interest).
+constexpr int kSpecMaxS = 10;
+
+// Count of bounded waits that gave up (read and cleared by hc_wait_timeouts()).
+__device__ unsigned int g_expm_wait_timeouts;
+constexpr uint32_t kGridWaitLimit = 1u << 22;  // polls of ~64 ns: a quarter of a second
+
+// Grid-wide barrier of a cooperative launch (every CTA is resident, so every
+// arrival comes), split in two so that a CTA can work between arriving and
+// waiting. `count` is zeroed by the host before the launch. Bounded: a CTA
+// that gives up counts it in g_expm_wait_timeouts and goes on.
+__device__ __forceinline__ void grid_arrive(unsigned int* count) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's partial maximum is visible to every CTA
+    atomicAdd(count, 1u);
+  }
+}
+
+__device__ __forceinline__ void grid_wait(unsigned int* count) {
+  if (threadIdx.x == 0) {
+    bool ok = false;
+    for (uint32_t i = 0; i < kGridWaitLimit; ++i) {
+      unsigned int seen;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(count) : "memory");
+      if (seen >= gridDim.x) {
+        ok = true;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!ok) atomicAdd(&g_expm_wait_timeouts, 1u);
+  }
+  __syncthreads();
+}
+
+// T18 forward, one thread per matrix, grid-stride over the batch, with the
+// scaling exponent per matrix (partial == nullptr) or, for the reference's
+// global scaling, from the partial maxima of ||A||_1 of a previous norm pass.
+template <int N>
+__global__ void __launch_bounds__(kExpmThreads) expm_t18_tm_fwd_kernel(const float* __restrict__ A,
+                                                                       float* __restrict__ E, int64_t batch,
+                                                                       const float* __restrict__ partial,
+                                                                       int nparts, int vec) {
+  const int s_glob = partial ? global_exponent(partial, nparts, kTheta18) : 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t mat = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; mat < batch; mat += stride) {
+    float a[N][N];
+    tm_load<N>(A, mat, vec != 0, a);
+    const int s = partial ? s_glob : scaling_exponent(tm_norm1<N>(a), kTheta18);
+    tm_scale<N>(a, pow2_neg(s));
+    float t[N][N];
+    tm_t18<N>(a, t);
+    for (int i = 0; i < s; ++i) tm_mm<N>(t, t, t);
+    tm_store<N>(E, mat, vec != 0, t);
+  }
+}
+
+// T18 forward with the reference's global scaling in ONE launch, one thread
+// per matrix (batch <= gridDim.x * blockDim.x): every CTA writes the maximum
+// ||A||_1 of its matrices to partial[blockIdx.x] and arrives at a grid barrier
+// (the launch is cooperative); while the barrier completes each thread forms
+// the powers A^2, A^3, A^6 of its matrix unscaled; every CTA then reduces all
+// partials to the batch's exponent s. Scaling by 2^-s commutes with every
+// rounded product and sum of those powers (power-of-two factors; for
+// s <= kSpecMaxS nothing overflows or becomes subnormal), so scaling them by
+// 2^-2s, 2^-3s, 2^-6s gives bit for bit the powers of A / 2^s; for larger s
+// the powers are formed again from A / 2^s.
+template <int N>
+__global__ void __launch_bounds__(kExpmThreads) expm_t18_tm_coop_kernel(const float* __restrict__ A,
+                                                                        float* __restrict__ E, int64_t batch,
+                                                                        float* __restrict__ partial,
+                                                                        unsigned int* __restrict__ arrive,
+                                                                        int vec) {
+  __shared__ float wmax[kExpmThreads / 32];
+  const int64_t mat = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool live = mat < batch;
+  float a[N][N];
+  tm_load<N>(A, live ? mat : 0, vec != 0, a);
+  float m = live ? tm_norm1<N>(a) : 0.f;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int w = 0; w < kExpmThreads / 32; ++w) b = fmaxf(b, wmax[w]);
+    partial[blockIdx.x] = b;
+  }
+  grid_arrive(arrive);
+  float p2[N][N], p3[N][N], p6[N][N];
+  tm_powers<N>(a, p2, p3, p6);
+  grid_wait(arrive);
+  float g = 0.f;
+  for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += blockDim.x) g = fmaxf(g, __ldcg(partial + i));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) g = fmaxf(g, __shfl_xor_sync(kFull, g, o));
+  __syncthreads();  // wmax is reused
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = g;
+  __syncthreads();
+  float b = 0.f;
+  for (int w = 0; w < kExpmThreads / 32; ++w) b = fmaxf(b, wmax[w]);
+  const int s = scaling_exponent(b, kTheta18);
+  if (!live) return;
+  tm_scale<N>(a, pow2_neg(s));
+  if (s <= kSpecMaxS) {
+    tm_scale<N>(p2, pow2_neg(2 * s));
+    tm_scale<N>(p3, pow2_neg(3 * s));
+    tm_scale<N>(p6, pow2_neg(6 * s));
+  } else {
+    tm_powers<N>(a, p2, p3, p6);
+  }
+  float t[N][N];
+  tm_t18_tail<N>(a, p2, p3, p6, t);
+  for (int i = 0; i < s; ++i) tm_mm<N>(t, t, t);
+  tm_store<N>(E, mat, vec != 0, t);
+}
+
+// T18 backward, one thread per matrix: the adjoint Frechet derivative
+// L(A^T, G) in forward mode, bitwise the result of expm_t18_bwd_kernel. The
+// (X, dX) pairs need ~230 live floats, so CTAs are small and each thread
+// stays close to the 255-register limit.
+constexpr int kExpmTmBwdThreads = 128;
+
+template <int N>
+__global__ void __launch_bounds__(kExpmTmBwdThreads) expm_t18_tm_bwd_kernel(const float* __restrict__ A,
+                                                                            const float* __restrict__ Gr,
+                                                                            float* __restrict__ dA, int64_t batch,
+                                                                            const float* __restrict__ partial,
+                                                                            int nparts, int vec) {
+  // The matrix loads go out first, so that their latency overlaps the
+  // reduction of the partial maxima (which ends in a CTA barrier).
+  const int64_t mat = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool live = mat < batch;
+  float at[N][N], e[N][N];
+  {
+    float a[N][N];
+    tm_load<N>(A, live ? mat : 0, vec != 0, a);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) at[i][j] = a[j][i];
+  }
+  tm_load<N>(Gr, live ? mat : 0, vec != 0, e);
+  const int s_glob = partial ? global_exponent(partial, nparts, kTheta18) : 0;
+  if (!live) return;
+  int s = s_glob;
+  if (!partial) {  // ||A||_1 as the max row sum of A^T, summed as norm1_from_transpose does
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float r = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) r += fabsf(at[i][j]);
+      m = fmaxf(m, r);
+    }
+    s = scaling_exponent(m, kTheta18);
+  }
+  const float sc = pow2_neg(s);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      at[i][j] *= sc;
+      e[i][j] *= sc;
+    }
+  float t[N][N], dt[N][N];
+  tm_t18_d<N>(at, e, t, dt);
+  for (int i = 0; i < s; ++i) tm_mm_d<N>(t, dt, t, dt, t, dt);
+  tm_store<N>(dA, mat, vec != 0, dt);
+}
+
 template <int N>
 __global__ void __launch_bounds__(kExpmThreads) expm_pade_fwd_kernel(const float* __restrict__ A,
                                                                      float* __restrict__ E, int64_t batch) {
@@ -620,6 +1056,94 @@ int launch_norm_partials(const float* A, int64_t batch, int n, float* scratch, i
   return launch_status();
 }
 
+// ---- the thread-per-matrix forward (n <= 4)
+// Its global-scaling launch is cooperative: at most the CTAs that can be
+// resident at once (occupancy x SMs), and at most kMaxNormParts - 1 of them
+// so that the partials and the barrier counter fit the scratch of the
+// two-kernel path. The partial maxima it leaves (one per CTA) are the ones
+// hc_expm_t18_bwd mode 2 reads, so both use t18_parts().
+constexpr int kTmMaxN = 4;
+
+template <int N>
+int tm_blocks_per_sm() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, expm_t18_tm_coop_kernel<N>, kExpmThreads, 0) !=
+          cudaSuccess ||
+      nb <= 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (dev < 64) cached[dev] = nb;
+  return nb;
+}
+
+int tm_coop_grid(int64_t batch, int n) {
+  int nb = 0;
+  switch (n) {
+    case 1: nb = tm_blocks_per_sm<1>(); break;
+    case 2: nb = tm_blocks_per_sm<2>(); break;
+    case 3: nb = tm_blocks_per_sm<3>(); break;
+    default: nb = tm_blocks_per_sm<4>(); break;
+  }
+  if (nb <= 0) nb = 1;  // no device to ask (CPU-only process): a grid of SMs
+  int64_t grid = (batch + kExpmThreads - 1) / kExpmThreads;
+  grid = std::min<int64_t>(grid, static_cast<int64_t>(nb) * sm_count());
+  grid = std::min<int64_t>(grid, kMaxNormParts - 1);
+  return static_cast<int>(std::max<int64_t>(grid, 1));
+}
+
+// Partial maxima of the global-scaling forward (and of the backward's norm
+// pass): one per CTA of the cooperative forward for n <= 4, one per CTA of
+// the norm kernel otherwise.
+int t18_parts(int64_t batch, int n) { return n <= kTmMaxN ? tm_coop_grid(batch, n) : norm_parts(batch, n); }
+
+// Scratch words: the partials, plus the barrier counter of the cooperative
+// launch for n <= 4.
+int64_t t18_scratch_words(int64_t batch, int n) { return t18_parts(batch, n) + (n <= kTmMaxN ? 1 : 0); }
+
+template <int N>
+int launch_tm_fwd(const float* A, float* E, int64_t batch, float* scratch, int parts, bool global, cudaStream_t st) {
+  const int vec = aligned16(A) && aligned16(E) ? 1 : 0;
+  const int64_t full_grid = (batch + kExpmThreads - 1) / kExpmThreads;
+  if (!global) {
+    expm_t18_tm_fwd_kernel<N><<<static_cast<unsigned>(full_grid), kExpmThreads, 0, st>>>(A, E, batch, nullptr, 0,
+                                                                                        vec);
+    return launch_status();
+  }
+  if (full_grid > parts) {  // more matrices than resident threads: norm pass, then the grid-stride kernel
+    if (int rc = launch_norm_partials(A, batch, N, scratch, parts, st)) return rc;
+    expm_t18_tm_fwd_kernel<N><<<parts, kExpmThreads, 0, st>>>(A, E, batch, scratch, parts, vec);
+    return launch_status();
+  }
+  unsigned int* arrive = reinterpret_cast<unsigned int*>(scratch + parts);
+  if (cudaMemsetAsync(arrive, 0, sizeof(unsigned int), st) != cudaSuccess) {
+    cudaGetLastError();
+    return HC_ERR_LAUNCH;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(parts), 1, 1);
+  cfg.blockDim = dim3(kExpmThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, expm_t18_tm_coop_kernel<N>, A, E, batch, scratch, arrive, vec) != cudaSuccess) {
+    cudaGetLastError();
+    return HC_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
 }  // namespace
 }  // namespace hc
 
@@ -627,7 +1151,7 @@ using namespace hc;
 
 extern "C" int64_t hc_expm_t18_scratch_words(int64_t batch, int n) {
   if (batch < 0 || n < 1 || n > 8) return 0;
-  return norm_parts(batch, n);
+  return t18_scratch_words(batch, n);
 }
 
 extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, float* scratch,
@@ -636,11 +1160,25 @@ extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, f
   int rc = check(A, E, batch, n);
   if (rc || batch == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n <= kTmMaxN) {
+    int parts = 0;
+    if (!per_matrix) {
+      parts = t18_parts(batch, n);
+      if (!scratch || scratch_words < t18_scratch_words(batch, n)) return HC_ERR_SCRATCH;
+      if (!aligned4(scratch)) return HC_ERR_ALIGNMENT;
+    }
+    switch (n) {
+      case 1: return launch_tm_fwd<1>(A, E, batch, scratch, parts, !per_matrix, st);
+      case 2: return launch_tm_fwd<2>(A, E, batch, scratch, parts, !per_matrix, st);
+      case 3: return launch_tm_fwd<3>(A, E, batch, scratch, parts, !per_matrix, st);
+      default: return launch_tm_fwd<4>(A, E, batch, scratch, parts, !per_matrix, st);
+    }
+  }
   const float* partial = nullptr;
   int parts = 0;
   if (!per_matrix) {
-    parts = norm_parts(batch, n);
-    if (!scratch || scratch_words < parts) return HC_ERR_SCRATCH;
+    parts = t18_parts(batch, n);
+    if (!scratch || scratch_words < t18_scratch_words(batch, n)) return HC_ERR_SCRATCH;
     if (!aligned4(scratch)) return HC_ERR_ALIGNMENT;
     rc = launch_norm_partials(A, batch, n, scratch, parts, st);
     if (rc) return rc;
@@ -664,14 +1202,28 @@ extern "C" int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_
   const float* partial = nullptr;
   int parts = 0;
   if (per_matrix != 1) {
-    parts = norm_parts(batch, n);
-    if (!scratch || scratch_words < parts) return HC_ERR_SCRATCH;
+    parts = t18_parts(batch, n);
+    if (!scratch || scratch_words < t18_scratch_words(batch, n)) return HC_ERR_SCRATCH;
     if (!aligned4(scratch)) return HC_ERR_ALIGNMENT;
     if (per_matrix == 0) {  // mode 2: the forward's partial maxima of this A are already in scratch
       rc = launch_norm_partials(A, batch, n, scratch, parts, st);
       if (rc) return rc;
     }
     partial = scratch;
+  }
+  if (n <= kTmMaxN) {
+    const int vec = aligned16(A) && aligned16(G) && aligned16(dA) ? 1 : 0;
+    const dim3 grid(static_cast<unsigned>((batch + kExpmTmBwdThreads - 1) / kExpmTmBwdThreads), 1, 1);
+#define L(NN) \
+  expm_t18_tm_bwd_kernel<NN><<<grid, kExpmTmBwdThreads, 0, st>>>(A, G, dA, batch, partial, parts, vec)
+    switch (n) {
+      case 1: L(1); break;
+      case 2: L(2); break;
+      case 3: L(3); break;
+      default: L(4); break;
+    }
+#undef L
+    return launch_status();
   }
   const dim3 grid = expm_grid(batch, n);
 #define L(NN) expm_t18_bwd_kernel<NN><<<grid, kExpmThreads, 0, st>>>(A, G, dA, batch, partial, parts)
@@ -768,3 +1320,18 @@ extern "C" int hc_expm_t18_fwd_noalloc(const float* A, float* E, int64_t batch, 
 #undef L
   return launch_status();
 }
+
+namespace hc {
+unsigned int expm_take_timeouts(bool reset) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_expm_wait_timeouts, sizeof(v)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (reset && v != 0) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_expm_wait_timeouts, &z, sizeof(z));
+  }
+  return v;
+}
+}  // namespace hc

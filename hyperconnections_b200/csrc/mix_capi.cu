@@ -225,7 +225,8 @@ extern "C" int hc_wait_timeouts(unsigned int* count, int reset) {
   const bool r = reset != 0;
   *count = mix_warp_take_timeouts_f32(r) + mix_warp_take_timeouts_f16(r) + mix_warp_take_timeouts_bf16(r) +
            rw_fwd_take_timeouts_f32(r) + rw_fwd_take_timeouts_f16(r) + rw_fwd_take_timeouts_bf16(r) +
-           rw_bwd_take_timeouts_f32(r) + rw_bwd_take_timeouts_f16(r) + rw_bwd_take_timeouts_bf16(r);
+           rw_bwd_take_timeouts_f32(r) + rw_bwd_take_timeouts_f16(r) + rw_bwd_take_timeouts_bf16(r) +
+           expm_take_timeouts(r);
   return HC_OK;
 }
 

@@ -179,3 +179,33 @@ def test_t18_backward_reuses_forward_partial_maxima():
                                        words, 2, s), "bwd mode 2")
         torch.cuda.synchronize()
         assert torch.equal(d0, d2)
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 4])
+def test_t18_forward_one_thread_per_matrix_is_bitwise_the_row_per_lane_kernel(n):
+    """For n <= 4 the T18 forward runs one matrix per thread (a cooperative
+    single launch when the batch fits the resident threads, else a norm pass
+    and a grid-stride kernel). hc_expm_t18_fwd_noalloc still runs the
+    row-per-lane kernels; the two must agree bit for bit: batch exponent 0, a
+    few squarings, more than kSpecMaxS = 10 squarings (the powers formed after
+    the barrier) and a batch larger than the resident threads."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(n)
+    cases = [(4000, 0.2), (50000, 3.0), (3000, 2.0e4), (200000, 1.5)]
+    for batch, scale in cases:
+        A = (scale * torch.randn(batch, n, n, generator=g)).to(DEVICE)
+        words = lib.hc_expm_t18_scratch_words(batch, n)
+        scratch = torch.empty(words, device=DEVICE)
+        s = torch.cuda.current_stream().cuda_stream
+        E_tm, E_row = torch.empty_like(A), torch.empty_like(A)
+        _lib.check(lib.hc_expm_t18_fwd(A.data_ptr(), E_tm.data_ptr(), batch, n, scratch.data_ptr(), words, 0, s),
+                   "hc_expm_t18_fwd")
+        _lib.check(lib.hc_expm_t18_fwd_noalloc(A.data_ptr(), E_row.data_ptr(), batch, n, s),
+                   "hc_expm_t18_fwd_noalloc")
+        torch.cuda.synchronize()
+        finite = torch.isfinite(E_row)
+        assert torch.equal(torch.isfinite(E_tm), finite)
+        assert torch.equal(E_tm[finite], E_row[finite]), (batch, scale)
+    assert _lib.wait_timeouts(reset=True) == 0
