@@ -1137,7 +1137,16 @@ int launch_tm_fwd(const float* A, float* E, int64_t batch, float* scratch, int p
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, expm_t18_tm_coop_kernel<N>, A, E, batch, scratch, arrive, vec) != cudaSuccess) {
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, expm_t18_tm_coop_kernel<N>, A, E, batch, scratch, arrive, vec);
+  if (e == cudaErrorCooperativeLaunchTooLarge) {
+    // fewer SMs usable than the device reports (an MPS share, for one): the
+    // two-launch form needs no co-residency and writes the same partials
+    cudaGetLastError();
+    if (int rc = launch_norm_partials(A, batch, N, scratch, parts, st)) return rc;
+    expm_t18_tm_fwd_kernel<N><<<parts, kExpmThreads, 0, st>>>(A, E, batch, scratch, parts, vec);
+    return launch_status();
+  }
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return HC_ERR_LAUNCH;
   }
