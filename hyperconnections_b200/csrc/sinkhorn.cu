@@ -12,12 +12,13 @@
 //   exp           dH = dX_0 * X_0
 // (the autograd rules of the reference's divisions and sums, applied per step).
 //
-// One thread owns one matrix in registers. A CTA stages its 128 matrices
-// through shared memory so that global loads and stores are coalesced. Up to
-// kSkLinearIters iterations the backward keeps the row and column sums of
-// every iteration and rebuilds the iterates in reverse (linear time); beyond
-// that it recomputes the forward prefix X_{k-1} for each step k from X_0
-// (iters^2 / 2 half-steps, no stored iterates).
+// A group of lanes owns a matrix, one row per lane (column sums by shuffles);
+// a CTA stages its matrices through shared memory so that global loads and
+// stores are coalesced. Up to kSkLinearIters iterations the backward keeps
+// the row and column sums of every iteration and rebuilds the iterates in
+// reverse (linear time); beyond that one thread per matrix recomputes the
+// forward prefix X_{k-1} for each step k from X_0 (iters^2 / 2 half-steps,
+// no stored iterates).
 #include "common.cuh"
 
 namespace hc {
@@ -66,30 +67,6 @@ template <int N>
 __device__ __forceinline__ void stage_out(float* __restrict__ g, const float* sm, int64_t first, int cnt) {
   float* dst = g + first * (N * N);
   for (int i = threadIdx.x; i < cnt * N * N; i += blockDim.x) dst[i] = sm[(i / (N * N)) * sk_pitch<N>() + i % (N * N)];
-}
-
-template <int N>
-__global__ void __launch_bounds__(kSkThreads) sinkhorn_fwd_kernel(const float* __restrict__ H, float* __restrict__ P,
-                                                                  int64_t batch, int iters) {
-  __shared__ float sm[kSkThreads * sk_pitch<N>()];
-  const int64_t first = static_cast<int64_t>(blockIdx.x) * kSkThreads;
-  const int cnt = static_cast<int>(batch - first < kSkThreads ? batch - first : kSkThreads);
-  stage_in<N>(H, sm, first, cnt);
-  __syncthreads();
-  if (threadIdx.x < cnt) {
-    float* row = sm + threadIdx.x * sk_pitch<N>();
-    float x[N * N], r[N], c[N];
-#pragma unroll
-    for (int k = 0; k < N * N; ++k) x[k] = expf(row[k]);
-    for (int it = 0; it < iters; ++it) {
-      row_normalize<N>(x, r);
-      col_normalize<N>(x, c);
-    }
-#pragma unroll
-    for (int k = 0; k < N * N; ++k) row[k] = x[k];
-  }
-  __syncthreads();
-  stage_out<N>(P, sm, first, cnt);
 }
 
 template <int N>
@@ -156,90 +133,160 @@ __global__ void __launch_bounds__(kSkThreads) sinkhorn_bwd_kernel(const float* _
 }
 
 // Backward in linear time for iters <= kSkLinearIters: the forward is run
-// once, keeping every iteration's row sums r_k and column sums c_k (2n floats
-// per iteration, in local memory); the backward then walks the steps in
-// reverse, rebuilding the iterates from the final X by multiplication,
-// Y_k = X_k c_k (columns) and X_{k-1} = Y_k r_k (rows), instead of
-// recomputing each prefix from X_0. The rebuilt iterates differ from the
-// forward's by a few units in the last place after 20 iterations, far inside
-// fp32 gradient accuracy; X_iters itself and X_0 = exp(H) are exact.
+// once, keeping every iteration's row sums r_k and column sums c_k (in local
+// memory); the backward then walks the steps in reverse, rebuilding the
+// iterates from the final X by multiplication, Y_k = X_k c_k (columns) and
+// X_{k-1} = Y_k r_k (rows), instead of recomputing each prefix from X_0. The
+// rebuilt iterates differ from the forward's by a few units in the last place
+// after 20 iterations, far inside fp32 gradient accuracy; X_iters itself and
+// X_0 = exp(H) are exact.
 constexpr int kSkLinearIters = 32;
 
+// ------------------------------------------------ one lane per row
+// A group of G lanes (G = n rounded up to a power of two) owns a matrix, lane
+// r its row r: a row sum is local, a column sum a log2(G)-step xor-shuffle
+// tree across the group. n to 8 times the threads of one thread per matrix,
+// and an n times shorter chain of divisions per thread. Lanes r >= n keep a
+// zero row and skip the row division (no 0/0); their column contributions
+// are zeros. The shuffles run on all 32 lanes, so lanes without a matrix
+// (past the batch) compute on a zero-filled copy and store nothing.
+template <int N> struct SkGroup {
+  static constexpr int G = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8;
+  static constexpr int kMats = kSkThreads / G;  // matrices per CTA
+};
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < G; o <<= 1) v += __shfl_xor_sync(kFull, v, o, G);
+  return v;
+}
+
+// Row r of matrix (first + m) from the CTA's staged copy, zeros outside.
 template <int N>
-__global__ void __launch_bounds__(kSkThreads) sinkhorn_bwd_linear_kernel(const float* __restrict__ H,
-                                                                         const float* __restrict__ G,
-                                                                         float* __restrict__ dH, int64_t batch,
-                                                                         int iters) {
-  __shared__ float sm[kSkThreads * sk_pitch<N>()];
-  const int64_t first = static_cast<int64_t>(blockIdx.x) * kSkThreads;
-  const int cnt = static_cast<int>(batch - first < kSkThreads ? batch - first : kSkThreads);
-  float x0[N * N], g[N * N];
+__device__ __forceinline__ void sk_row_in(const float* sm, int m, int r, int cnt, float (&v)[N]) {
+  const bool ok = m < cnt && r < N;
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = ok ? sm[m * sk_pitch<N>() + r * N + j] : 0.f;
+}
+
+template <int N>
+__device__ __forceinline__ void sk_row_out(float* sm, int m, int r, int cnt, const float (&v)[N]) {
+  if (m >= cnt || r >= N) return;
+#pragma unroll
+  for (int j = 0; j < N; ++j) sm[m * sk_pitch<N>() + r * N + j] = v[j];
+}
+
+// One Sinkhorn iteration on this lane's row; returns the row sum and the
+// column sums (every lane of the group gets all of them).
+template <int N, int G>
+__device__ __forceinline__ float sk_iter_row(float (&x)[N], bool real_row, float (&c)[N]) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) s += x[j];
+  if (real_row) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[j] = x[j] / s;
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    c[j] = group_sum<G>(x[j]);
+    x[j] = x[j] / c[j];
+  }
+  return s;
+}
+
+template <int N>
+__global__ void __launch_bounds__(kSkThreads) sinkhorn_fwd_rows_kernel(const float* __restrict__ H,
+                                                                       float* __restrict__ P, int64_t batch,
+                                                                       int iters) {
+  constexpr int G = SkGroup<N>::G, M = SkGroup<N>::kMats;
+  __shared__ float sm[M * sk_pitch<N>()];
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * M;
+  const int cnt = static_cast<int>(batch - first < M ? batch - first : M);
   stage_in<N>(H, sm, first, cnt);
   __syncthreads();
-  float* row = sm + threadIdx.x * sk_pitch<N>();
-  if (threadIdx.x < cnt) {
+  const int m = threadIdx.x / G, r = threadIdx.x % G;
+  const bool real_row = m < cnt && r < N;
+  float x[N];
+  sk_row_in<N>(sm, m, r, cnt, x);
 #pragma unroll
-    for (int k = 0; k < N * N; ++k) x0[k] = expf(row[k]);
+  for (int j = 0; j < N; ++j) x[j] = real_row ? expf(x[j]) : 0.f;
+  for (int it = 0; it < iters; ++it) {
+    float c[N];
+    sk_iter_row<N, G>(x, real_row, c);
   }
   __syncthreads();
-  stage_in<N>(G, sm, first, cnt);
+  sk_row_out<N>(sm, m, r, cnt, x);
   __syncthreads();
-  if (threadIdx.x < cnt) {
+  stage_out<N>(P, sm, first, cnt);
+}
+
+// Linear-time backward (iters <= kSkLinearIters) in the row-per-lane layout:
+// the forward keeps this lane's row sum and all column sums per iteration.
+template <int N>
+__global__ void __launch_bounds__(kSkThreads) sinkhorn_bwd_rows_kernel(const float* __restrict__ H,
+                                                                       const float* __restrict__ Gr,
+                                                                       float* __restrict__ dH, int64_t batch,
+                                                                       int iters) {
+  constexpr int G = SkGroup<N>::G, M = SkGroup<N>::kMats;
+  __shared__ float sm[M * sk_pitch<N>()];
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * M;
+  const int cnt = static_cast<int>(batch - first < M ? batch - first : M);
+  const int m = threadIdx.x / G, r = threadIdx.x % G;
+  const bool real_row = m < cnt && r < N;
+  float x0[N], g[N];
+  stage_in<N>(H, sm, first, cnt);
+  __syncthreads();
+  sk_row_in<N>(sm, m, r, cnt, x0);
 #pragma unroll
-    for (int k = 0; k < N * N; ++k) g[k] = row[k];
-    float rs[kSkLinearIters][N], cs[kSkLinearIters][N];
-    float x[N * N];
+  for (int j = 0; j < N; ++j) x0[j] = real_row ? expf(x0[j]) : 0.f;
+  __syncthreads();
+  stage_in<N>(Gr, sm, first, cnt);
+  __syncthreads();
+  sk_row_in<N>(sm, m, r, cnt, g);
+  float rs[kSkLinearIters], cs[kSkLinearIters][N];
+  float x[N];
 #pragma unroll
-    for (int q = 0; q < N * N; ++q) x[q] = x0[q];
-    for (int it = 0; it < iters; ++it) {
-      float r[N], c[N];
-      row_normalize<N>(x, r);
-      col_normalize<N>(x, c);
+  for (int j = 0; j < N; ++j) x[j] = x0[j];
+  for (int it = 0; it < iters; ++it) {
+    float c[N];
+    rs[it] = sk_iter_row<N, G>(x, real_row, c);
 #pragma unroll
-      for (int i = 0; i < N; ++i) {
-        rs[it][i] = r[i];
-        cs[it][i] = c[i];
-      }
-    }
-    for (int k = iters - 1; k >= 0; --k) {  // x holds X_{k+1}
-      float r[N], c[N], y[N * N];
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        r[i] = rs[k][i];
-        c[i] = cs[k][i];
-      }
-      // column step: dY_ij = (g_ij - sum_l g_lj X_lj) / c_j
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        float t = 0.f;
-#pragma unroll
-        for (int l = 0; l < N; ++l) t += g[l * N + j] * x[l * N + j];
-#pragma unroll
-        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - t) / c[j];
-      }
-#pragma unroll
-      for (int i = 0; i < N; ++i)
-#pragma unroll
-        for (int j = 0; j < N; ++j) y[i * N + j] = x[i * N + j] * c[j];
-      // row step: dX_ij = (dY_ij - sum_l dY_il Y_il) / r_i
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        float t = 0.f;
-#pragma unroll
-        for (int l = 0; l < N; ++l) t += g[i * N + l] * y[i * N + l];
-#pragma unroll
-        for (int j = 0; j < N; ++j) g[i * N + j] = (g[i * N + j] - t) / r[i];
-      }
-#pragma unroll
-      for (int i = 0; i < N; ++i)
-#pragma unroll
-        for (int j = 0; j < N; ++j) x[i * N + j] = y[i * N + j] * r[i];
-    }
-#pragma unroll
-    for (int q = 0; q < N * N; ++q) row[q] = g[q] * x0[q];
+    for (int j = 0; j < N; ++j) cs[it][j] = c[j];
   }
+  for (int k = iters - 1; k >= 0; --k) {  // x holds row r of X_{k+1}
+    const float rr = real_row ? rs[k] : 1.f;
+    float c[N], y[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) c[j] = cs[k][j];
+    // column step: dY_ij = (g_ij - sum_l g_lj X_lj) / c_j
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float t = group_sum<G>(g[j] * x[j]);
+      g[j] = real_row ? (g[j] - t) / c[j] : 0.f;
+      y[j] = x[j] * c[j];
+    }
+    // row step: dX_ij = (dY_ij - sum_l dY_il Y_il) / r_i
+    float t = 0.f;
+#pragma unroll
+    for (int l = 0; l < N; ++l) t += g[l] * y[l];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      g[j] = (g[j] - t) / rr;
+      x[j] = y[j] * rr;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) g[j] *= x0[j];
+  __syncthreads();
+  sk_row_out<N>(sm, m, r, cnt, g);
   __syncthreads();
   stage_out<N>(dH, sm, first, cnt);
+}
+
+unsigned rows_grid(int64_t batch, int mats_per_cta) {
+  return static_cast<unsigned>((batch + mats_per_cta - 1) / mats_per_cta);
 }
 
 int check_sk(const void* a, const void* b, int64_t batch, int n, int iters) {
@@ -273,9 +320,10 @@ using namespace hc;
 extern "C" int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, int iters, void* stream) {
   int rc = check_sk(H, P, batch, n, iters);
   if (rc || batch == 0) return rc;
-  const unsigned grid = static_cast<unsigned>((batch + kSkThreads - 1) / kSkThreads);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define L(NN) sinkhorn_fwd_kernel<NN><<<grid, kSkThreads, 0, st>>>(H, P, batch, iters)
+#define L(NN)                                                                                   \
+  sinkhorn_fwd_rows_kernel<NN><<<rows_grid(batch, SkGroup<NN>::kMats), kSkThreads, 0, st>>>(H, P, batch, \
+                                                                                            iters)
   HC_SK_SWITCH(n, L)
 #undef L
   return launch_status();
@@ -290,7 +338,9 @@ extern "C" int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_
   const unsigned grid = static_cast<unsigned>((batch + kSkThreads - 1) / kSkThreads);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (iters <= kSkLinearIters) {
-#define L(NN) sinkhorn_bwd_linear_kernel<NN><<<grid, kSkThreads, 0, st>>>(H, G, dH, batch, iters)
+#define L(NN)                                                                                        \
+  sinkhorn_bwd_rows_kernel<NN><<<rows_grid(batch, SkGroup<NN>::kMats), kSkThreads, 0, st>>>(H, G, dH, batch, \
+                                                                                             iters)
     HC_SK_SWITCH(n, L)
 #undef L
     return launch_status();
