@@ -25,8 +25,9 @@
 // stores). A token stays on one consumer warp, so the backward's per-token
 // sums (grad_Phi / grad_H, grad_alpha, grad_beta, the projection terms)
 // accumulate in registers over all slices and fold with one warp
-// transpose-reduce; at n >= 5 with sliced tokens the sums go to a per-warp
-// Gram in shared memory a block of rows at a time (the blocked backward).
+// transpose-reduce; at n >= 5 with sliced tokens or the projection the sums
+// go to a per-warp Gram in shared memory a block of rows at a time (the
+// blocked backward).
 //
 // Every wait is bounded (kWaitLimit polls). A warp that gives up counts it in
 // a device counter (hc_wait_timeouts) and raises the CTA's abort flag; all
@@ -976,13 +977,16 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const Params& pr
 // The Gram is M = A B^T over the slice's elements, with A's rows g_0..g_{n-1}
 // and B's rows x_0..x_{n-1}, each extended by g_u and f in the fused step.
 // Then grad_Phi_ij = M_ij, and in the fused step grad_alpha_j = M_nj and
-// grad_beta_i = M_in.
-// The blocked path runs at n >= 5 for tokens cut into slices, without the
-// projection. Measured on B200: +1-7% there; the single pass with every sum
-// in registers is faster for whole tokens (by 16% at n = 8, D = 512) and with
-// the projection (by 11-15%, sliced or not).
-constexpr bool bwd_blocked_n(int n, bool proj) { return n >= 5 && !proj; }
-inline bool bwd_blocked(int n, bool proj, int ns) { return bwd_blocked_n(n, proj) && ns > 1; }
+// grad_beta_i = M_in; with the projection (stream_mix_add with v) the finish
+// forms its terms from M alone (bwd_gram_finish).
+// The blocked path runs at n >= 5 for tokens cut into slices, and for every
+// token with the projection (whose extra sums the finish derives from the
+// plain Gram). Measured on B200: +1-7% for sliced tokens; with the projection
+// +3-17% over the single pass (which spills at n = 6, 8), except -1.5% at
+// n = 7, D = 768; for whole tokens without the projection the single pass
+// with every sum in registers stays faster (by 16% at n = 8, D = 512).
+constexpr bool bwd_blocked_n(int n) { return n >= 5; }
+inline bool bwd_blocked(int n, bool proj, int ns) { return bwd_blocked_n(n) && (ns > 1 || proj); }
 
 template <int N, bool FUSED>
 struct GramShape {
@@ -992,10 +996,10 @@ struct GramShape {
   static constexpr int RB = 32 / NA;              // rows per block: RB * NA <= 32 sums
 };
 
-// Pass A: grad_x_j = sum_i Phi_ij g_i (+ alpha_j g_u) and grad_f = beta^T g
-// over one slice; same arithmetic as bwd_slice.
-template <typename T, typename P, int N, bool FUSED, int W>
-__device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, false>& pr,
+// Pass A: grad_x_j = sum_i Phi_ij g_i (+ v_j c^T g) (+ alpha_j g_u) and
+// grad_f = beta^T g over one slice; same arithmetic as bwd_slice.
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+__device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
                                                 const uint8_t* gsb, const uint8_t* usb, int pitch, int64_t t,
                                                 int64_t d0, int len, int lane) {
   using Wd = Word<T>;
@@ -1020,6 +1024,16 @@ __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokPa
 #pragma unroll
       for (int r = 0; r < N; ++r) Wd::get(gw_[r].w[w], ge[r]);
       if constexpr (FUSED) Wd::get(uw.w[w], gue);
+      float bt[K];
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float s = 0.f;
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2) s = fmaf(ge[i2][e], pr.cc[i2], s);
+          bt[e] = s;
+        }
+      }
 #pragma unroll
       for (int j = 0; j < N; ++j) {
         float o[K];
@@ -1028,6 +1042,7 @@ __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokPa
           float s = 0.f;
 #pragma unroll
           for (int i2 = 0; i2 < N; ++i2) s = fmaf(pr.phi[i2 * N + j], ge[i2][e], s);
+          if constexpr (PROJ) s = fmaf(pr.vv[j], bt[e], s);
           if constexpr (FUSED) s = fmaf(pr.al[j], gue[e], s);
           o[e] = s;
         }
@@ -1124,17 +1139,62 @@ __device__ __forceinline__ void bwd_gram_slice(float* gram, const uint8_t* gsb, 
 }
 
 // The token's parameter gradients from its Gram, then the Gram cleared for
-// the warp's next token.
-template <int N, bool FUSED>
-__device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, float* gram, int64_t t, int lane) {
+// the warp's next token. With the projection the extra sums are linear in
+// the plain Gram M = G X^T: rho_i = sum_d g_i v^T x = sum_j v_j M_ij and
+// bp_j = sum_d (c^T g) x_j = sum_i c_i M_ij, so grad_Phi_ij = M_ij - v_j rho_i
+// and grad_v_j = rho_j - sum_i Phi_ij rho_i + bp_j (reference
+// ops/stream_mix_small_nb.py:379-384). Register arrays are indexed with
+// constants only (selects over the runtime row and column).
+template <typename P, int N, bool FUSED, bool PROJ>
+__device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
+                                                float* gram, int64_t t, int lane) {
   using G = GramShape<N, FUSED>;
   constexpr int NA = G::NA;
   __syncwarp();
+  float rho[PROJ ? N : 1];
+  if constexpr (PROJ) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float r = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) r = fmaf(pr.vv[j], gram[i * NA + j], r);
+      rho[i] = r;
+    }
+  }
   if (a.grad_phi) {
 #pragma unroll
     for (int q = 0; q < (N * N + 31) / 32; ++q) {
       const int k = lane + 32 * q;
-      if (k < N * N) a.grad_phi[t * (N * N) + k] = gram[(k / N) * NA + k % N];
+      if (k < N * N) {
+        const int i = k / N, j = k % N;
+        float s = gram[i * NA + j];
+        if constexpr (PROJ) {
+          float vj = 0.f, ri = 0.f;
+#pragma unroll
+          for (int q2 = 0; q2 < N; ++q2) {
+            vj = q2 == j ? pr.vv[q2] : vj;
+            ri = q2 == i ? rho[q2] : ri;
+          }
+          s = fmaf(-vj, ri, s);
+        }
+        a.grad_phi[t * (N * N) + k] = s;
+      }
+    }
+  }
+  if constexpr (PROJ) {
+    if (a.grad_v != nullptr && lane < N) {
+      const int j = lane;
+      float ptr = 0.f, bp = 0.f, rj = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float pij = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < N; ++jj) pij = jj == j ? pr.phi[i * N + jj] : pij;
+        ptr = fmaf(pij, rho[i], ptr);
+        bp = fmaf(pr.cc[i], gram[i * NA + j], bp);
+        rj = i == j ? rho[i] : rj;
+      }
+      a.grad_v[t * N + j] = (rj - ptr) + bp;
     }
   }
   if constexpr (FUSED) {
@@ -1197,7 +1257,6 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
     float2 acc2[PAIRS ? L::kAcc : 1];
     float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
     if constexpr (BLOCKED) {
-      static_assert(!PROJ, "the blocked path has no projection terms");
       for (int k = lane; k < GramShape<N, FUSED>::SIZE; k += 32) gram[k] = 0.f;
       __syncwarp();
     }
@@ -1239,9 +1298,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
           const uint8_t* us = sb + 2 * nreg + tt * rowb;
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
           if constexpr (BLOCKED) {
-            bwd_grads_slice<T, P, N, FUSED, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
+            bwd_grads_slice<T, P, N, FUSED, PROJ, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
             bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
-            if (p == ns - 1) bwd_gram_finish<N, FUSED>(a, gram, t, lane);
+            if (p == ns - 1) bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
           } else {
             if constexpr (PAIRS) {
               bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
@@ -1410,10 +1469,14 @@ int launch_bwd_kernel(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, 
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ>
 int launch_bwd_one(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
-  if constexpr (bwd_blocked_n(N, PROJ)) {
-    if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+  if constexpr (bwd_blocked_n(N) && PROJ) {
+    return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+  } else {
+    if constexpr (bwd_blocked_n(N)) {
+      if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+    }
+    return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, block, a, s);
   }
-  return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, block, a, s);
 }
 
 template <typename T, typename P, bool FUSED, bool PROJ>
