@@ -759,6 +759,31 @@ def time_stream_mix(device, B, N, D, dtype, proj, steps, warmup):
     return time_launches(device, [fwd, bwd], steps, warmup)
 
 
+def time_pade(device, B, n, steps, warmup):
+    """Pade [7/7] matrix exponential (the replacement of torch.linalg.matrix_exp
+    in the CGHC layer) forward + backward over B matrices of the expm workload:
+    the two kernels through the C-ABI, and for context torch.linalg.matrix_exp
+    with autograd on the same GPU."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    A, G = (t.to(device) for t in expm_workload(B, n, seed=3))
+    E, dA = torch.empty_like(A), torch.empty_like(A)
+    st = torch.cuda.current_stream(device).cuda_stream
+
+    def kernels():
+        _lib.check(lib.hc_expm_pade_fwd(A.data_ptr(), E.data_ptr(), B, n, st), "hc_expm_pade_fwd")
+        _lib.check(lib.hc_expm_pade_bwd(A.data_ptr(), G.data_ptr(), dA.data_ptr(), B, n, st), "hc_expm_pade_bwd")
+
+    def eager():
+        At = A.detach().requires_grad_(True)
+        torch.autograd.grad(torch.linalg.matrix_exp(At), At, G)
+
+    k_ms, t_ms = time_launches(device, [kernels, eager], steps, warmup)
+    return {"sweep": "expm_pade", "batch": B, "n": n, "kernels_ms": k_ms, "matrices_per_s": B / (k_ms * 1e-3),
+            "torch_matrix_exp_gpu_ms": t_ms}
+
+
 def time_generator(device, T, n, steps, warmup):
     """CGHC's generator (conservative + PSD dissipation, the reference's
     default type, scalar dt) forward + backward over T tokens: the kernel pair
@@ -811,7 +836,7 @@ def run_sweep(args):
     the fused fwd+bwd GB/s and its fraction of the HBM peak; one line per
     (n, m, D, projection) for the two-phase read / mix-write kernels; the
     Sinkhorn-Knopp projection at n = 2, 4, 8; then one line per n for the
-    per-token batched expm (16,384 matrices, fwd+bwd)."""
+    per-token batched expm (16,384 matrices, fwd+bwd), T18 and Pade."""
     _, _, local = dist_env()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -864,6 +889,8 @@ def run_sweep(args):
         ms = float(np.mean(time_expm(device, steps, args.warmup, B=TOKENS, n=n)))
         print(json.dumps({"sweep": "expm_t18", "batch": TOKENS, "n": n, "ms_per_step": ms,
                           "matrices_per_s": TOKENS / (ms * 1e-3)}), flush=True)
+    for n in SWEEP_N:
+        print(json.dumps(time_pade(device, TOKENS, n, steps, args.warmup)), flush=True)
 
 
 def main():
