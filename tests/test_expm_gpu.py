@@ -209,3 +209,43 @@ def test_t18_forward_one_thread_per_matrix_is_bitwise_the_row_per_lane_kernel(n)
         assert torch.equal(torch.isfinite(E_tm), finite)
         assert torch.equal(E_tm[finite], E_row[finite]), (batch, scale)
     assert _lib.wait_timeouts(reset=True) == 0
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_t18_unaligned_buffers_take_the_scalar_path_bitwise(n):
+    """Matrices of 16 and 64 bytes are read and written with 16-byte vector
+    accesses when the buffers allow it; buffers that start 4 bytes off a
+    16-byte boundary go through scalar accesses. Both must give the same bits
+    (forward, and backward in both scaling modes)."""
+    from hyperconnections_b200 import _lib
+
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(40 + n)
+    B = 5000
+    A = (1.5 * torch.randn(B, n, n, generator=g)).to(DEVICE)
+    G = torch.randn(B, n, n, generator=g).to(DEVICE)
+    s = torch.cuda.current_stream().cuda_stream
+    words = lib.hc_expm_t18_scratch_words(B, n)
+    scratch = torch.empty(words, device=DEVICE)
+
+    def off(t):  # same values, base pointer 4 bytes past a 16-byte boundary
+        buf = torch.empty(t.numel() + 1, device=DEVICE)
+        v = buf[1:].view(t.shape)
+        v.copy_(t)
+        return v
+
+    def run(A_, G_):
+        E, dA0, dA2 = (off(torch.zeros_like(A)) if A_.data_ptr() % 16 else torch.empty_like(A) for _ in range(3))
+        _lib.check(lib.hc_expm_t18_fwd(A_.data_ptr(), E.data_ptr(), B, n, scratch.data_ptr(), words, 0, s), "fwd")
+        _lib.check(lib.hc_expm_t18_bwd(A_.data_ptr(), G_.data_ptr(), dA2.data_ptr(), B, n, scratch.data_ptr(),
+                                       words, 2, s), "bwd mode 2")
+        _lib.check(lib.hc_expm_t18_bwd(A_.data_ptr(), G_.data_ptr(), dA0.data_ptr(), B, n, scratch.data_ptr(),
+                                       words, 1, s), "bwd per matrix")
+        torch.cuda.synchronize()
+        return [t.clone() for t in (E, dA2, dA0)]
+
+    Ao, Go = off(A), off(G)
+    assert Ao.data_ptr() % 16 == 4 and A.data_ptr() % 16 == 0
+    for got, want in zip(run(Ao, Go), run(A, G)):
+        assert torch.equal(got, want)
+    assert _lib.wait_timeouts(reset=True) == 0
