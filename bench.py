@@ -305,25 +305,28 @@ class ExpmRunner:
         self._check(rc, "hc_expm_t18_bwd")
 
 
-def time_expm(device, steps, warmup, B=EXPM_BATCH, n=EXPM_N):
+def time_expm(device, steps, warmup, B=EXPM_BATCH, n=EXPM_N, split=False):
     """Device time of one expm forward + backward over B resident matrices
-    (C-ABI launches), L2 flushed between steps; ms per step."""
+    (C-ABI launches), L2 flushed between steps; ms per step (and, with
+    split=True, also the forward's ms per step)."""
     runner = ExpmRunner(device, B, n)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     for _ in range(warmup):
         runner.fwd()
         runner.bwd()
     torch.cuda.synchronize(device)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
         flush.fill_(float(i))
         evs[i][0].record()
         runner.fwd()
-        runner.bwd()
         evs[i][1].record()
+        runner.bwd()
+        evs[i][2].record()
     torch.cuda.synchronize(device)
     del flush
-    return [e[0].elapsed_time(e[1]) for e in evs]
+    step = [e[0].elapsed_time(e[2]) for e in evs]
+    return (step, [e[0].elapsed_time(e[1]) for e in evs]) if split else step
 
 
 def time_expm_api(device, steps, warmup):
@@ -521,10 +524,11 @@ def run_b200(args):
     fb, bb = fused_bytes(TOKENS, N_STREAMS, BLOCK)
     value = world * (fb + bb) / (step_ms_max * 1e-3) / 1e9
 
-    expm_ms = time_expm(device, max(5, min(args.steps, 50)), max(3, args.warmup))
+    expm_ms, expm_fwd_ms = time_expm(device, max(5, min(args.steps, 50)), max(3, args.warmup), split=True)
     expm_step = float(np.mean(expm_ms))
     expm_step_max = max_over_ranks(expm_step, world, device)
     expm_rate = world * EXPM_BATCH / (expm_step_max * 1e-3)
+    expm_fwd_max = max_over_ranks(float(np.mean(expm_fwd_ms)), world, device)
     expm_api_ms = max_over_ranks(time_expm_api(device, 20, 3), world, device)
 
     # 20 steps: the pipeline's fill and drain (one transfer each that nothing
@@ -564,6 +568,8 @@ def run_b200(args):
             "expm": {"metric": "batched expm fwd+bwd matrices/s", "value": expm_rate, "unit": "matrices/s",
                      "ms_per_step": expm_step_max, "batch": EXPM_BATCH, "n": EXPM_N,
                      "scaling": "global (reference semantics)",
+                     "fwd": {"value": world * EXPM_BATCH / (expm_fwd_max * 1e-3), "unit": "matrices/s",
+                             "ms_per_step": expm_fwd_max},
                      "api": {"value": world * EXPM_BATCH / (expm_api_ms * 1e-3), "unit": "matrices/s",
                              "ms_per_step": expm_api_ms,
                              "path": "hyperconnections_b200.ops.expm_t18 + autograd (host-bound)"}},
