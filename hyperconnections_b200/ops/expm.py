@@ -3,10 +3,12 @@
 ``expm_t18(A)`` keeps the reference's algorithm and signature
 (hyperconnections/ops/expm.py:65-106): the optimised degree-18 Taylor
 polynomial of Bader, Blanes and Casas (2019) with scaling and squaring and ONE
-scaling exponent for the whole batch, from max ||A||_1 (expm.py:81-85). The
-forward and the backward are one kernel launch each after a batch-max kernel;
-the backward is the adjoint Frechet derivative of the same approximant
-(what the reference gets from autograd through its graph).
+scaling exponent for the whole batch, from max ||A||_1 (expm.py:81-85). For
+n <= 4 the forward is one cooperative kernel launch (the batch maximum, a
+grid barrier and T18 in one kernel; larger batches or n take a batch-max
+kernel first); the backward is one launch that reuses the forward's partial
+maxima, the adjoint Frechet derivative of the same approximant (what the
+reference gets from autograd through its graph).
 
 Differences from the reference, both deliberate:
 * the squaring loop runs s times; the reference stops after 8 squarings
