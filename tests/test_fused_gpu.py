@@ -3,10 +3,11 @@
 Expected values: the CPU oracle (oracle.stream_mix.fused_*), and golden
 fixtures produced by the reference's own composition (read einsum
 cghc.py:410 -> write einsum :417 -> stream_mix_add :449) in float32 on
-bf16-exact inputs. Tolerances: 1e-5 relative in fp32; in bf16, 2e-2 absolute
-plus 2^-7 |ref| (the output rounding of values >= 8, whose bf16 half-ulp alone
-exceeds 2e-2) against an fp32-accumulated oracle of the same bf16 inputs.
-Parameter gradients, fp32 sums over D, are held to 1e-5 relative.
+bf16-exact inputs. Tolerances: 1e-5 relative in fp32; in bf16 / fp16,
+2e-2 / 1e-2 absolute wherever |ref| < 8 against an fp32-accumulated oracle of
+the same half-precision inputs, and half an ulp more where |ref| >= 8
+(tests/parity.py; those elements are counted separately). Parameter
+gradients, fp32 sums over D, are held to 1e-5 relative.
 """
 
 import numpy as np
@@ -15,6 +16,7 @@ import torch
 
 from oracle import stream_mix as omix
 from tests.conftest import load_golden
+from tests.parity import assert_half
 
 pytestmark = pytest.mark.gpu
 
@@ -72,9 +74,8 @@ def check(u, x_out, grads, inputs, stream_tol, rel):
             err = np.abs(np64(got) - ref).max() if ref.size else 0.0
             bound = tol * max(1.0, np.abs(ref).max() if ref.size else 0.0)
             assert err <= bound, f"{what}: max err {err:.3e} > {bound:.3e}"
-        else:  # half: tol absolute, plus 2^-7 |ref| for the output rounding of large values
-            excess = np.abs(np64(got) - ref) - (tol + 2.0**-7 * np.abs(ref))
-            assert excess.max(initial=-1.0) <= 0, f"{what}: exceeds bound by {excess.max():.3e}"
+        else:  # half: the absolute parity bar where |ref| < 8, + half-ulp above
+            assert_half(got, ref, what)
 
     close(u, ru, "u", stream_tol)
     close(x_out, rx, "x_out", stream_tol)
@@ -100,7 +101,7 @@ def test_fused_half(dtype, n, D):
     u, x_out, grads = run(*inputs)
     assert u.dtype == dtype and x_out.dtype == dtype and grads[0].dtype == dtype
     assert grads[2].dtype == torch.float32
-    check(u, x_out, grads, inputs, 2e-2, rel=False)
+    check(u, x_out, grads, inputs, None, rel=False)
 
 
 FUSED = load_golden("fused.npz")
@@ -119,7 +120,7 @@ def test_golden_reference_composition(case, dtype):
         if dtype == torch.float32:
             assert np.abs(np64(got) - r).max() <= 1e-5 * max(1.0, np.abs(r).max()), name
         else:
-            assert (np.abs(np64(got) - r) - (2e-2 + 2.0**-7 * np.abs(r))).max() <= 0, name
+            assert_half(got, r, name)
     for got, name in zip(grads[2:], ("grad_H", "grad_alpha", "grad_beta")):
         r = ref(name)
         assert np.abs(np64(got) - r).max() <= 1e-5 * max(1.0, np.abs(r).max()), name
@@ -137,7 +138,7 @@ def test_fused_full_size_workload():
     assert u.shape == (16, 1024, D) and x_out.shape == (16, 1024, n, D)
     torch.autograd.backward([u, x_out], [shp(g_u), shp(g_x)])
     grads = [t.grad.reshape(T, *t.shape[2:]) for t in ts]
-    check(u.reshape(T, D), x_out.reshape(T, n, D), grads, (x, f, H, alpha, beta, g_u, g_x), 2e-2, rel=False)
+    check(u.reshape(T, D), x_out.reshape(T, n, D), grads, (x, f, H, alpha, beta, g_u, g_x), None, rel=False)
 
 
 def test_fused_linearity_and_identity():
@@ -185,5 +186,5 @@ def test_fused_many_tokens_per_cta(n, D, T, dtype):
     if dtype == torch.float32:
         check(u, x_out, grads, inputs, 1e-5, rel=True)
     else:
-        check(u, x_out, grads, inputs, 2e-2, rel=False)
+        check(u, x_out, grads, inputs, None, rel=False)
     assert _lib.wait_timeouts() == 0
