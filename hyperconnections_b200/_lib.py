@@ -36,7 +36,9 @@ _SIGNATURES = {
     "hc_error_string": (ctypes.c_char_p, [_c_int]),
     "hc_abi_version": (_c_int, []),
     "hc_wait_timeouts": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
-    "hc_set_mix_tuning": (_c_int, [_c_int, _c_int, _c_int]),
+    "hc_timeout_status": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
+    "hc_debug_set_mix_tuning": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
+    "hc_debug_set_wait_limit": (_c_int, [ctypes.c_uint]),
     "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
     "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_t18_fwd_noalloc": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp]),
@@ -63,7 +65,7 @@ _SIGNATURES = {
     "hc_mix_write_bwd": (_c_int, [_vp] * 11 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
 }
 
-EXPECTED_ABI_VERSION = 5
+EXPECTED_ABI_VERSION = 6
 
 _lib: Optional[ctypes.CDLL] = None
 _load_error: Optional[str] = None
@@ -129,9 +131,28 @@ def stream_of(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+HC_ERR_TIMEOUT = 8
+
+
 def wait_timeouts(reset: bool = False) -> int:
     """Number of bounded kernel waits that gave up on the current device
-    (synchronises the device)."""
+    (synchronises the device). reset=True also clears the sticky status that
+    makes every entry point return HC_ERR_TIMEOUT after a give-up."""
     count = ctypes.c_uint(0)
     check(lib().hc_wait_timeouts(ctypes.byref(count), 1 if reset else 0), "hc_wait_timeouts")
     return int(count.value)
+
+
+def timeout_status() -> int:
+    """Give-ups recorded so far by kernels that have reached them (no
+    synchronisation)."""
+    count = ctypes.c_uint(0)
+    check(lib().hc_timeout_status(ctypes.byref(count)), "hc_timeout_status")
+    return int(count.value)
+
+
+def raise_if_timed_out(what: str) -> None:
+    """RuntimeError when a kernel has already recorded a give-up (checked at
+    the end of a backward pass by the autograd wrappers; no synchronisation)."""
+    if timeout_status():
+        check(HC_ERR_TIMEOUT, what)

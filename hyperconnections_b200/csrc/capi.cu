@@ -11,8 +11,11 @@ extern "C" const char* hc_error_string(int code) {
     case HC_ERR_ALIGNMENT: return "a float32 pointer is not 4-byte aligned";
     case HC_ERR_SCRATCH: return "scratch buffer missing or too small";
     case HC_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case HC_ERR_TIMEOUT:
+      return "a bounded wait inside an earlier kernel gave up, so that launch's outputs are incomplete "
+             "(cleared by hc_wait_timeouts with reset)";
     default: return "unknown hcops status code";
   }
 }
 
-extern "C" int hc_abi_version(void) { return 5; }
+extern "C" int hc_abi_version(void) { return 6; }

@@ -9,6 +9,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "../../include/hcops.h"
@@ -250,4 +251,56 @@ inline int dtype_size(int dt) {
 // hc_wait_timeouts() with those of the ring kernels.
 unsigned int expm_take_timeouts(bool reset);
 
+// ------------------------------------------------------ bounded-wait status
+// Every spin-wait in the kernels polls at most a fixed number of times. A wait
+// that gives up leaves its kernel's outputs incomplete; the kernel counts the
+// event in a per-translation-unit device counter and in ONE word of pinned,
+// device-mapped host memory shared by the process (status.cu). Every entry
+// point that launches work reads that word first and returns HC_ERR_TIMEOUT
+// while it is non-zero, until hc_wait_timeouts(..., reset = 1) clears it, so
+// a caller learns of the give-up at its next call (like a sticky CUDA error).
+constexpr uint32_t kWaitPolls = 1u << 22;  // default poll limit of every data wait
+
+// Device-visible address of the status word, mapped on first use (never while
+// stream s is capturing a graph); nullptr when it cannot be mapped.
+unsigned int* timeout_word(cudaStream_t s);
+// HC_ERR_TIMEOUT when some kernel has reported a give-up, else HC_OK; never
+// maps the word (a plain host read of it when it exists).
+int pending_timeout();
+// Clears the status word (hc_wait_timeouts with reset).
+void clear_timeout_word();
+// Poll limit of the data waits: kWaitPolls unless hc_debug_set_wait_limit
+// lowered it. The exit drains of the rings always use kWaitPolls.
+uint32_t wait_poll_limit();
+
+// Ring geometry overrides of hc_debug_set_mix_tuning (0 = automatic), read
+// atomically at every launch.
+struct MixTuning {
+  int stage_bytes;  // target bytes of an item of several small tokens
+  int stages;       // stages of the ring
+  int warps;        // consumer warps per CTA
+  int producers;    // producer lanes of warp 0
+};
+MixTuning mix_tuning();
+
+__device__ __forceinline__ void report_timeout(unsigned int* counter, unsigned int* word) {
+  atomicAdd(counter, 1u);
+  if (word) atomicAdd_system(word, 1u);
+}
+
+// NVTX range around one C-ABI call (visible in Nsight Systems / ncu's NVTX
+// filter; a no-op branch when no tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
 }  // namespace hc
+
+// First statement of every entry point that launches work: an NVTX range
+// named after it, then the sticky give-up status of earlier launches.
+#define HC_ENTRY(name)                  \
+  const ::hc::NvtxRange hc_nvtx_(name); \
+  if (const int hc_pending_ = ::hc::pending_timeout()) return hc_pending_

@@ -800,12 +800,14 @@ constexpr int kSpecMaxS = 10;
 
 // Count of bounded waits that gave up (read and cleared by hc_wait_timeouts()).
 __device__ unsigned int g_expm_wait_timeouts;
-constexpr uint32_t kGridWaitLimit = 1u << 22;  // polls of ~64 ns: a quarter of a second
 
 // Grid-wide barrier of a cooperative launch (every CTA is resident, so every
 // arrival comes), split in two so that a CTA can work between arriving and
-// waiting. `count` is zeroed by the host before the launch. Bounded: a CTA
-// that gives up counts it in g_expm_wait_timeouts and goes on.
+// waiting. `count` is zeroed by the host before the launch. Bounded (`limit`
+// polls of ~64 ns; kWaitPolls is a quarter of a second): a CTA that gives up
+// counts it in g_expm_wait_timeouts and in the library's status word (the
+// next entry point call returns HC_ERR_TIMEOUT) and goes on with the partial
+// maxima it has seen, so that batch's exponent may be too small.
 __device__ __forceinline__ void grid_arrive(unsigned int* count) {
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -814,10 +816,10 @@ __device__ __forceinline__ void grid_arrive(unsigned int* count) {
   }
 }
 
-__device__ __forceinline__ void grid_wait(unsigned int* count) {
+__device__ __forceinline__ void grid_wait(unsigned int* count, uint32_t limit, unsigned int* status) {
   if (threadIdx.x == 0) {
     bool ok = false;
-    for (uint32_t i = 0; i < kGridWaitLimit; ++i) {
+    for (uint32_t i = 0; i < limit; ++i) {
       unsigned int seen;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(count) : "memory");
       if (seen >= gridDim.x) {
@@ -826,7 +828,7 @@ __device__ __forceinline__ void grid_wait(unsigned int* count) {
       }
       __nanosleep(64);
     }
-    if (!ok) atomicAdd(&g_expm_wait_timeouts, 1u);
+    if (!ok) report_timeout(&g_expm_wait_timeouts, status);
   }
   __syncthreads();
 }
@@ -868,7 +870,8 @@ __global__ void __launch_bounds__(kExpmThreads) expm_t18_tm_coop_kernel(const fl
                                                                         float* __restrict__ E, int64_t batch,
                                                                         float* __restrict__ partial,
                                                                         unsigned int* __restrict__ arrive,
-                                                                        int vec) {
+                                                                        int vec, uint32_t wait_limit,
+                                                                        unsigned int* status) {
   __shared__ float wmax[kExpmThreads / 32];
   const int64_t mat = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const bool live = mat < batch;
@@ -887,7 +890,7 @@ __global__ void __launch_bounds__(kExpmThreads) expm_t18_tm_coop_kernel(const fl
   grid_arrive(arrive);
   float p2[N][N], p3[N][N], p6[N][N];
   tm_powers<N>(a, p2, p3, p6);
-  grid_wait(arrive);
+  grid_wait(arrive, wait_limit, status);
   float g = 0.f;
   for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += blockDim.x) g = fmaxf(g, __ldcg(partial + i));
 #pragma unroll
@@ -1137,7 +1140,8 @@ int launch_tm_fwd(const float* A, float* E, int64_t batch, float* scratch, int p
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, expm_t18_tm_coop_kernel<N>, A, E, batch, scratch, arrive, vec);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, expm_t18_tm_coop_kernel<N>, A, E, batch, scratch, arrive, vec,
+                                           wait_poll_limit(), timeout_word(st));
   if (e == cudaErrorCooperativeLaunchTooLarge) {
     // fewer SMs usable than the device reports (an MPS share, for one): the
     // two-launch form needs no co-residency and writes the same partials
@@ -1165,6 +1169,7 @@ extern "C" int64_t hc_expm_t18_scratch_words(int64_t batch, int n) {
 
 extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, float* scratch,
                                int64_t scratch_words, int per_matrix, void* stream) {
+  HC_ENTRY("hc_expm_t18_fwd");
   if (per_matrix != 0 && per_matrix != 1) return HC_ERR_BAD_SIZE;
   int rc = check(A, E, batch, n);
   if (rc || batch == 0) return rc;
@@ -1202,6 +1207,7 @@ extern "C" int hc_expm_t18_fwd(const float* A, float* E, int64_t batch, int n, f
 
 extern "C" int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch, int n,
                                float* scratch, int64_t scratch_words, int per_matrix, void* stream) {
+  HC_ENTRY("hc_expm_t18_bwd");
   if (per_matrix < 0 || per_matrix > 2) return HC_ERR_BAD_SIZE;
   int rc = check(A, dA, batch, n);
   if (rc || batch == 0) return rc;
@@ -1242,6 +1248,7 @@ extern "C" int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_
 }
 
 extern "C" int hc_expm_pade_fwd(const float* A, float* E, int64_t batch, int n, void* stream) {
+  HC_ENTRY("hc_expm_pade_fwd");
   int rc = check(A, E, batch, n);
   if (rc || batch == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1254,6 +1261,7 @@ extern "C" int hc_expm_pade_fwd(const float* A, float* E, int64_t batch, int n, 
 
 extern "C" int hc_expm_pade_bwd(const float* A, const float* G, float* dA, int64_t batch, int n,
                                 void* stream) {
+  HC_ENTRY("hc_expm_pade_bwd");
   int rc = check(A, dA, batch, n);
   if (rc || batch == 0) return rc;
   if (!G) return HC_ERR_NULL_POINTER;
@@ -1313,8 +1321,10 @@ int noalloc_scratch(float** out) {
 extern "C" int hc_expm_t18_fwd_noalloc(const float* A, float* E, int64_t batch, int n, void* stream) {
   int rc = check(A, E, batch, n);
   if (rc || batch == 0) return rc;
+  // norm_parts() caps the partial maxima at kMaxNormParts (the norm kernel
+  // strides over the batch), the size of the array: any batch up to the
+  // 2^34-matrix bound fits.
   const int parts = norm_parts(batch, n);
-  if (parts > kMaxNormParts) return HC_ERR_SCRATCH;  // the array holds kMaxNormParts partial maxima
   float* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;

@@ -351,6 +351,7 @@ extern "C" int hc_cghc_generator_fwd(const float* M, const float* lc, const floa
                                      const float* S, const float* ld, float* A, int64_t T, int n, int vec_dt,
                                      int flags, float dt_min_c, float dt_max_c, float dt_min_d, float dt_max_d,
                                      void* stream) {
+  HC_ENTRY("hc_cghc_generator_fwd");
   GenArgs a{};
   a.M = M; a.lc = lc; a.ld = ld; a.R = R; a.dpre = dpre; a.S = S; a.A = A; a.T = T;
   a.lo_c = dt_min_c; a.hi_c = dt_max_c; a.lo_d = dt_min_d; a.hi_d = dt_max_d;
@@ -372,6 +373,7 @@ extern "C" int hc_cghc_generator_bwd(const float* M, const float* lc, const floa
                                      float* dR, float* ddpre, float* dS, float* dld, int64_t T, int n, int vec_dt,
                                      int flags, float dt_min_c, float dt_max_c, float dt_min_d, float dt_max_d,
                                      void* stream) {
+  HC_ENTRY("hc_cghc_generator_bwd");
   GenArgs a{};
   a.M = M; a.lc = lc; a.ld = ld; a.R = R; a.dpre = dpre; a.S = S; a.G = G; a.T = T;
   a.dM = dM; a.dlc = dlc; a.dld = dld; a.dR = dR; a.ddpre = ddpre; a.dS = dS;

@@ -103,6 +103,7 @@ using namespace hc;
 extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, const void* v,
                                  void* out, int64_t B, int n, int64_t D, int stream_dtype,
                                  int param_dtype, void* stream) {
+  HC_ENTRY("hc_stream_mix_fwd");
   int rc = check_sizes(B, n, D, kBigMaxN);
   if (rc) return rc;
   rc = check_dtypes(stream_dtype, param_dtype);
@@ -135,6 +136,7 @@ extern "C" int hc_stream_mix_fwd(const void* Phi, const void* x, const void* Y, 
 extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, const void* v,
                                  void* grad_x, float* grad_Phi, float* grad_v, int64_t B, int n,
                                  int64_t D, int stream_dtype, int param_dtype, void* stream) {
+  HC_ENTRY("hc_stream_mix_bwd");
   int rc = check_sizes(B, n, D, kBigMaxN);
   if (rc) return rc;
   rc = check_dtypes(stream_dtype, param_dtype);
@@ -172,6 +174,7 @@ extern "C" int hc_stream_mix_bwd(const void* G, const void* Phi, const void* x, 
 extern "C" int hc_fused_fwd(const void* x, const void* f, const float* H, const float* alpha,
                             const float* beta, void* u, void* x_out, int64_t T, int n, int64_t D,
                             int stream_dtype, void* stream) {
+  HC_ENTRY("hc_fused_fwd");
   int rc = check_sizes(T, n, D);
   if (rc) return rc;
   if (dtype_size(stream_dtype) == 0) return HC_ERR_DTYPE;
@@ -194,6 +197,7 @@ extern "C" int hc_fused_bwd(const void* g_u, const void* g_x, const void* x, con
                             const float* H, const float* alpha, const float* beta, void* grad_x,
                             void* grad_f, float* grad_H, float* grad_alpha, float* grad_beta,
                             int64_t T, int n, int64_t D, int stream_dtype, void* stream) {
+  HC_ENTRY("hc_fused_bwd");
   int rc = check_sizes(T, n, D);
   if (rc) return rc;
   if (dtype_size(stream_dtype) == 0) return HC_ERR_DTYPE;
@@ -227,25 +231,6 @@ extern "C" int hc_wait_timeouts(unsigned int* count, int reset) {
            rw_fwd_take_timeouts_f32(r) + rw_fwd_take_timeouts_f16(r) + rw_fwd_take_timeouts_bf16(r) +
            rw_bwd_take_timeouts_f32(r) + rw_bwd_take_timeouts_f16(r) + rw_bwd_take_timeouts_bf16(r) +
            expm_take_timeouts(r);
-  return HC_OK;
-}
-
-// HC_PRODUCER_LANES (build flag, 0 = automatic) fixes the producer lanes of
-// every ring, for measurements.
-#ifndef HC_PRODUCER_LANES
-#define HC_PRODUCER_LANES 0
-#endif
-
-namespace hc {
-WarpTuning& warp_tuning() {
-  static WarpTuning t{0, 0, 0, HC_PRODUCER_LANES};
-  return t;
-}
-}  // namespace hc
-
-extern "C" int hc_set_mix_tuning(int stage_bytes, int stages, int warps) {
-  if (stage_bytes < 0 || stages < 0 || stages > kRingMaxStages || warps < 0 || warps >= kWarpMaxWarps)
-    return HC_ERR_BAD_SIZE;
-  hc::warp_tuning() = hc::WarpTuning{stage_bytes, stages, warps, hc::warp_tuning().producers};
+  if (r) clear_timeout_word();
   return HC_OK;
 }

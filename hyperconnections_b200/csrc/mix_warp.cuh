@@ -29,10 +29,12 @@
 // go to a per-warp Gram in shared memory a block of rows at a time (the
 // blocked backward).
 //
-// Every wait is bounded (kWaitLimit polls). A warp that gives up counts it in
-// a device counter (hc_wait_timeouts) and raises the CTA's abort flag; all
-// warps stop, and before the CTA exits one thread waits (bounded again) for
-// every copy the producer issued, so none lands after the CTA is gone.
+// Every wait is bounded (geo.wait_limit polls). A warp that gives up counts it
+// in a device counter and in the library's status word (the next entry point
+// call returns HC_ERR_TIMEOUT) and raises the CTA's abort flag; all warps
+// stop, and before the CTA exits one thread waits (bounded again, always with
+// the full kWaitPolls) for every copy the producer issued, so none lands after
+// the CTA is gone.
 #pragma once
 
 #include <algorithm>
@@ -80,7 +82,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr int kRingMaxStages = 32;  // stages of the per-CTA ring
 constexpr int kWarpMaxWarps = 16;   // producer + consumers
 
@@ -92,8 +93,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
@@ -173,6 +174,8 @@ struct WarpGeometry {
   int grid;         // CTAs
   int smem_bytes;   // dynamic shared memory per CTA
   int producers;    // lanes of warp 0 that issue fills (1 <= producers <= stages)
+  uint32_t wait_limit;  // polls of a data wait before it gives up
+  unsigned int* status; // the library's status word (device-mapped host memory), or nullptr
 };
 
 
@@ -298,8 +301,8 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
         for (int w = 0; w < Wg; ++w) {
           if (st.abort) return;
           if (k >= S) {
-            if (!warp_wait(&st.empty[s], ph ^ 1u)) {
-              atomicAdd(&g_mix_wait_timeouts, 1u);
+            if (!warp_wait(&st.empty[s], ph ^ 1u, geo.wait_limit)) {
+              report_timeout(&g_mix_wait_timeouts, geo.status);
               st.abort = 1;
               return;
             }
@@ -332,7 +335,7 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
     bool fail = false;
     if (act && !st.abort) {
       if (c.k >= S) {
-        fail = !warp_wait(&st.empty[c.s], c.ph ^ 1u);
+        fail = !warp_wait(&st.empty[c.s], c.ph ^ 1u, geo.wait_limit);
         if (!fail) fence_proxy_async_smem();
       }
       if (!fail) {
@@ -347,7 +350,7 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
       }
     }
     if (fail) {
-      atomicAdd(&g_mix_wait_timeouts, 1u);
+      report_timeout(&g_mix_wait_timeouts, geo.status);
       st.abort = 1;
     }
     if (__any_sync(mask, st.abort)) break;
@@ -363,7 +366,7 @@ __device__ __forceinline__ void ring_drain(RingState& st, int stages) {
   __syncthreads();
   if (threadIdx.x == 0)
     for (int s = 0; s < stages; ++s)
-      if (st.issued[s]) warp_wait(&st.full[s], st.last_parity[s]);
+      if (st.issued[s]) warp_wait(&st.full[s], st.last_parity[s], kWaitPolls);
 }
 
 // Consumer-side cursor over the ring: item index k, its stage and parity.
@@ -382,10 +385,11 @@ struct RingCursor {
 };
 
 // Consumer wait for its item: first until the producer has started this
-// item's fill (tag), then on the fill's phase. Bounded; warp-uniform result.
-__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur) {
+// item's fill (tag), then on the fill's phase. Bounded (`limit` polls each);
+// warp-uniform result.
+__device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& cur, uint32_t limit) {
   bool ok = false;
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (st.tag[cur.s] == cur.k) {
       ok = true;
       break;
@@ -394,7 +398,7 @@ __device__ __forceinline__ bool ring_wait_item(RingState& st, const RingCursor& 
     __nanosleep(32);
   }
   __threadfence_block();
-  if (ok) ok = warp_wait(&st.full[cur.s], cur.ph);
+  if (ok) ok = warp_wait(&st.full[cur.s], cur.ph, limit);
   return __all_sync(kFull, ok);
 }
 
@@ -763,9 +767,9 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, geo.wait_limit)) {
           if (lane == 0 && !st.abort) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
+            report_timeout(&g_mix_wait_timeouts, geo.status);
             st.abort = 1;
           }
           ok = false;
@@ -1270,9 +1274,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, geo.wait_limit)) {
           if (lane == 0 && !st.abort) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
+            report_timeout(&g_mix_wait_timeouts, geo.status);
             st.abort = 1;
           }
           ok = false;
@@ -1337,15 +1341,6 @@ inline int warp_rows(bool bwd, bool fused, int n) {
   return fused ? 2 * n + 2 : 2 * n;
 }
 
-// Tuning knobs (0 = automatic), set through hc_set_mix_tuning().
-struct WarpTuning {
-  int stage_bytes;  // target bytes of an item of several small tokens
-  int stages;       // stages of the ring
-  int warps;        // consumer warps per CTA
-  int producers;    // producer lanes (not part of the C ABI; fixed by a build flag)
-};
-WarpTuning& warp_tuning();
-
 // Geometry of the ring; false when the shape does not fit it.
 // Requires D % (16 / esize) == 0 and 16-byte aligned stream bases.
 //   * a token whose rows exceed max_stage is cut into slices (one bulk copy
@@ -1355,7 +1350,7 @@ WarpTuning& warp_tuning();
 inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
                           int num_sms, bool bwd) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
-  const WarpTuning tune = warp_tuning();
+  const MixTuning tune = mix_tuning();
   const int budget = 200 * 1024;
   const int64_t max_stage = 24 * 1024;
   // items of several small tokens: one bulk copy has a fixed cost, so small
@@ -1385,6 +1380,8 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   geo.producers = 1;
   geo.smem_bytes = stages * geo.stage_bytes;
   geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
+  geo.wait_limit = wait_poll_limit();
+  geo.status = nullptr;  // set by the launcher, which knows the stream
   return true;
 }
 
@@ -1393,7 +1390,7 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
 // computes). Measured best on B200 over D in 512..4096: 7 for sliced tokens;
 // for whole tokens 8 at n <= 4 and all 11 at n = 5, 6.
 inline void prefer_bwd_consumers(WarpGeometry& geo, int n) {
-  if (warp_tuning().warps > 0) return;
+  if (mix_tuning().warps > 0) return;
   if (geo.ns > 1) {
     geo.consumers = std::min(geo.consumers, 7);
   } else if (n <= 4) {
@@ -1409,8 +1406,9 @@ inline void prefer_bwd_consumers(WarpGeometry& geo, int n) {
 constexpr int kSmallFillBytes = 12 * 1024;
 constexpr int kManyFillLanes = 4;
 inline void prefer_producers(WarpGeometry& geo) {
-  if (warp_tuning().producers > 0) {
-    geo.producers = std::min(warp_tuning().producers, geo.stages);
+  const int fixed = mix_tuning().producers;
+  if (fixed > 0) {
+    geo.producers = std::min(fixed, geo.stages);
   } else if (geo.ns > 1 || geo.stage_bytes < kSmallFillBytes) {
     geo.producers = std::min(kManyFillLanes, geo.stages);
   }
@@ -1424,6 +1422,8 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
     geo.consumers = std::min(geo.consumers, cap - 1);
     if (cap > 8) prefer_bwd_consumers(geo, n);
     prefer_producers(geo);
+  } else if (mix_tuning().producers > 0) {
+    geo.producers = std::min(mix_tuning().producers, geo.stages);
   }
   return true;
 }
@@ -1442,7 +1442,9 @@ constexpr int fwd_lane_words(int n) { return n <= 4 ? 4 : 2; }
 constexpr int bwd_lane_words(int n, bool blocked) { return blocked || n == 5 || n == 6 ? 1 : 2; }
 
 template <typename T, typename P, bool FUSED, bool PROJ>
-int launch_mix_fwd_warp(int n, const WarpGeometry& geo, const MixFwdArgs& a, cudaStream_t s) {
+int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, cudaStream_t s) {
+  WarpGeometry geo = geo_in;
+  geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
@@ -1480,7 +1482,9 @@ int launch_bwd_one(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cud
 }
 
 template <typename T, typename P, bool FUSED, bool PROJ>
-int launch_mix_bwd_warp(int n, const WarpGeometry& geo, const MixBwdArgs& a, cudaStream_t s) {
+int launch_mix_bwd_warp(int n, const WarpGeometry& geo_in, const MixBwdArgs& a, cudaStream_t s) {
+  WarpGeometry geo = geo_in;
+  geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \

@@ -53,6 +53,7 @@ using namespace hc;
 
 extern "C" int hc_read_fwd(const float* R, const void* x, void* u, int64_t T, int n, int m, int64_t D,
                            int stream_dtype, void* stream) {
+  HC_ENTRY("hc_read_fwd");
   int rc = check_rw(T, n, m, D, stream_dtype);
   if (rc) return rc;
   if (T == 0 || D == 0) return HC_OK;
@@ -67,6 +68,7 @@ extern "C" int hc_read_fwd(const float* R, const void* x, void* u, int64_t T, in
 
 extern "C" int hc_read_bwd(const void* g_u, const float* R, const void* x, void* grad_x, float* grad_R, int64_t T,
                            int n, int m, int64_t D, int stream_dtype, void* stream) {
+  HC_ENTRY("hc_read_bwd");
   int rc = check_rw(T, n, m, D, stream_dtype);
   if (rc) return rc;
   if (T == 0) return HC_OK;
@@ -84,6 +86,7 @@ extern "C" int hc_read_bwd(const void* g_u, const float* R, const void* x, void*
 
 extern "C" int hc_mix_write_fwd(const float* H, const void* x, const float* W, const void* f, const float* v,
                                 void* out, int64_t T, int n, int m, int64_t D, int stream_dtype, void* stream) {
+  HC_ENTRY("hc_mix_write_fwd");
   int rc = check_rw(T, n, m, D, stream_dtype);
   if (rc) return rc;
   if (T == 0 || D == 0) return HC_OK;
@@ -101,6 +104,7 @@ extern "C" int hc_mix_write_fwd(const float* H, const void* x, const float* W, c
 extern "C" int hc_mix_write_bwd(const void* g, const float* H, const void* x, const float* W, const void* f,
                                 const float* v, void* grad_x, void* grad_f, float* grad_H, float* grad_W,
                                 float* grad_v, int64_t T, int n, int m, int64_t D, int stream_dtype, void* stream) {
+  HC_ENTRY("hc_mix_write_bwd");
   int rc = check_rw(T, n, m, D, stream_dtype);
   if (rc) return rc;
   if (T == 0) return HC_OK;

@@ -192,9 +192,9 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
       pr.load(a, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, geo.wait_limit)) {
           if (lane == 0 && !st.abort) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
+            report_timeout(&g_mix_wait_timeouts, geo.status);
             st.abort = 1;
           }
           ok = false;
@@ -441,9 +441,9 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
       pr.load(a, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
-        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur)) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, geo.wait_limit)) {
           if (lane == 0 && !st.abort) {
-            atomicAdd(&g_mix_wait_timeouts, 1u);
+            report_timeout(&g_mix_wait_timeouts, geo.status);
             st.abort = 1;
           }
           ok = false;
@@ -635,7 +635,9 @@ rw_bwd_generic_kernel(const RwArgs a, int n, int m, bool mixw) {
 inline bool rw_ring_supported(int n, int m) { return n >= 1 && n <= 8 && m >= 1 && m <= 4 && m <= n; }
 
 template <typename T, bool BWD, bool MIXW, bool PROJ, int N, int M>
-int rw_launch_one(const WarpGeometry& geo, const RwArgs& a, cudaStream_t s) {
+int rw_launch_one(const WarpGeometry& geo_in, const RwArgs& a, cudaStream_t s) {
+  WarpGeometry geo = geo_in;
+  geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   if constexpr (BWD) {
     auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ>;

@@ -318,6 +318,7 @@ int check_sk(const void* a, const void* b, int64_t batch, int n, int iters) {
 using namespace hc;
 
 extern "C" int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, int iters, void* stream) {
+  HC_ENTRY("hc_sinkhorn_fwd");
   int rc = check_sk(H, P, batch, n, iters);
   if (rc || batch == 0) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -331,6 +332,7 @@ extern "C" int hc_sinkhorn_fwd(const float* H, float* P, int64_t batch, int n, i
 
 extern "C" int hc_sinkhorn_bwd(const float* H, const float* G, float* dH, int64_t batch, int n, int iters,
                                void* stream) {
+  HC_ENTRY("hc_sinkhorn_bwd");
   int rc = check_sk(H, dH, batch, n, iters);
   if (rc || batch == 0) return rc;
   if (!G) return HC_ERR_NULL_POINTER;

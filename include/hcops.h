@@ -6,10 +6,23 @@
  *   - takes DEVICE pointers, element counts and a cudaStream_t passed as void*
  *     (NULL = legacy default stream);
  *   - enqueues its kernels on that stream and returns without synchronising;
- *   - allocates nothing and keeps no state between calls (scratch memory, where
- *     a path needs it, is passed in by the caller);
+ *   - allocates no device memory (scratch memory, where a path needs it, is
+ *     passed in by the caller) and keeps no per-call state;
  *   - returns HC_OK (0) or one of the HC_ERR_* codes below; hc_error_string()
  *     turns a code into text.
+ * Process-wide state is limited to the status of bounded waits (below) and
+ * the two hc_debug_* knobs.
+ *
+ * Bounded waits. Kernels that wait on each other's work (the bulk-copy ring
+ * of the stream-mixing kernels, the grid barrier of the cooperative expm
+ * forward) poll a bounded number of times. A wait that gives up leaves that
+ * launch's outputs incomplete; the kernel records it in one word of pinned,
+ * device-mapped host memory, and from then on every entry point that launches
+ * work returns HC_ERR_TIMEOUT without launching, until hc_wait_timeouts(..., 1)
+ * clears it (like a sticky CUDA error, the call after the failing one reports
+ * it). The word is mapped (cudaHostAlloc, 64 bytes, once per process) at the
+ * first launch of such a kernel on a stream that is not capturing a graph;
+ * make one call of each op before capturing it.
  *
  * Layouts are dense row-major with the token (batch) index outermost:
  *   streams  x, Y, out, grad_out, grad_x   [T, n, D]   stream dtype
@@ -42,6 +55,7 @@ extern "C" {
 #define HC_ERR_ALIGNMENT      5  /* a float32 pointer is not 4-byte aligned        */
 #define HC_ERR_SCRATCH        6  /* scratch buffer missing or too small            */
 #define HC_ERR_LAUNCH         7  /* the CUDA launch itself failed                  */
+#define HC_ERR_TIMEOUT        8  /* a bounded wait in an earlier launch gave up    */
 
 /* ---- dtype codes ---------------------------------------------------------- */
 #define HC_DTYPE_F32   0
@@ -56,19 +70,35 @@ const char* hc_error_string(int code);
 int hc_abi_version(void);
 
 /* Diagnostics: synchronises the current device, then stores in *count how
- * many bounded pipeline waits inside the stream-mixing kernels gave up since
- * the last reset (0 in a healthy run; a kernel that gives up leaves its
- * outputs incomplete and returns instead of spinning). reset != 0 clears the
- * counters. No reference counterpart (the reference's Triton kernels have no
- * such waits). */
+ * many bounded waits inside the kernels gave up since the last reset (0 in a
+ * healthy run; a kernel that gives up leaves its outputs incomplete and
+ * returns instead of spinning). reset != 0 clears the counters and the status
+ * word, after which the entry points launch again. No reference counterpart
+ * (the reference's Triton kernels have no such waits). */
 int hc_wait_timeouts(unsigned int* count, int reset);
 
-/* Performance tuning of the pipelined stream-mixing kernels, process-wide:
- * target bytes of one pipeline stage, stages per warp and warps per CTA; 0
- * keeps the automatic choice for that knob. Results do not depend on these
- * settings. No reference counterpart (the reference autotunes its Triton
- * block sizes, ops/stream_mix_small_nb.py:52-67). */
-int hc_set_mix_tuning(int stage_bytes, int stages, int warps);
+/* Non-blocking: the give-ups recorded in the status word so far (by kernels
+ * that have reached their give-up; no synchronisation, so a launch still
+ * running is not counted yet). 0 when no kernel with bounded waits has been
+ * launched. No reference counterpart. */
+int hc_timeout_status(unsigned int* count);
+
+/* DEBUG / BENCHMARK HOOK, process-wide and read at every launch: overrides
+ * the ring geometry of the pipelined stream-mixing kernels (target bytes of
+ * one item, stages, consumer warps, producer lanes of the fill warp; 0 keeps
+ * the automatic choice). Results do
+ * not depend on these settings; a launch on another thread sees either the
+ * old or the new values. Not for production use. No reference counterpart
+ * (the reference autotunes its Triton block sizes,
+ * ops/stream_mix_small_nb.py:52-67). */
+int hc_debug_set_mix_tuning(int stage_bytes, int stages, int warps, int producers);
+
+/* DEBUG / TEST HOOK, process-wide: the number of polls after which a data
+ * wait of the ring kernels and the grid barrier of the cooperative expm give
+ * up (0 restores the default of 2^22 polls, about a quarter of a second).
+ * Lowering it makes waits run out on purpose, to test the HC_ERR_TIMEOUT
+ * path; the ring's exit drain keeps the default. No reference counterpart. */
+int hc_debug_set_wait_limit(unsigned int polls);
 
 /* ===========================================================================
  * Batched matrix exponential, n <= 8, float32.
@@ -111,8 +141,8 @@ int hc_expm_t18_bwd(const float* A, const float* G, float* dA, int64_t batch,
  * ||A||_1, at most 1024 floats) lives in a fixed 4 KB device array inside the
  * library, which every GPU that loads the library keeps until exit. Limits:
  * the same batch bound as the other expm entry points (2^34 matrices, else
- * HC_ERR_BAD_SIZE); a batch that would need more partial maxima than the
- * array holds is rejected with HC_ERR_SCRATCH. The first call on a device
+ * HC_ERR_BAD_SIZE); every batch within it fits the array, since the norm pass
+ * strides over the batch with at most 1024 blocks. The first call on a device
  * looks up the array's device address once (cudaGetSymbolAddress); make that
  * first call before any stream capture. All calls share the one array and it
  * keeps the last call's contents; every slot a call reads is written earlier
