@@ -1,7 +1,9 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE's own
 code (pjjajal/hyperconnections) on the CPU of this container.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of pjjajal/hyperconnections>
+
+(or set HC_REFERENCE to that checkout's root)
 
 What runs, all from the reference checkout, unmodified:
   * expm_t18's Python body (hyperconnections/ops/expm.py:65-106) without its
@@ -365,6 +367,60 @@ def gen_layer(ref_path, out):
     np.savez_compressed(os.path.join(out, "layer.npz"), **rec)
 
 
+def gen_module(out):
+    """Whole CGHC layers of the reference (hyperconnections/cghc.py:14-457),
+    eager path, float32, wrapping a Linear: the layer's state_dict (its own
+    parameter names), a seeded input, the forward output, an upstream
+    gradient and the gradient of the input and of every trainable parameter.
+    Covers every generator family, the three projection modes, m = 1..4,
+    scalar and per-stream dt, learn_dt, biased heads and an affine RMSNorm.
+    Keys: "<case>/meta", "<case>/x", "<case>/g", "<case>/out", "<case>/grad_x",
+    "<case>/sd/<name>", "<case>/grad/<name>"."""
+    from hyperconnections.cghc import ContinuousGenHyperConnections as CGHC
+
+    configs = [  # (n, m, embed_dim, generator_type, projection, vec_dt, learn_dt, bias, affine)
+        (4, 1, 64, "conservative_psd_diss", "none", False, False, False, False),
+        (4, 2, 128, "conservative_diag_diss", "mean", False, False, False, False),
+        (6, 3, 96, "conservative_laplacian", "v", True, True, False, False),
+        (2, 1, 32, "conservative", "none", False, False, True, True),
+        (4, 4, 32, "psd_diss", "v", False, True, True, False),
+        (8, 2, 128, "laplacian", "mean", True, False, False, True),
+        (3, 1, 48, "diagonal_diss", "none", True, True, False, False),
+    ]
+    gen_codes = ["conservative", "psd_diss", "diagonal_diss", "laplacian", "conservative_diag_diss",
+                 "conservative_psd_diss", "conservative_laplacian"]
+    proj_codes = ["none", "mean", "v"]
+    rec = {}
+    for ci, (n, m, E, gen, proj, vec_dt, learn_dt, bias, affine) in enumerate(configs):
+        torch.manual_seed(5000 + ci)
+        inp = n * E // m
+        layer = CGHC(n, m, inp, E, torch.nn.Linear(E, E), dt=0.2, generator_type=gen, projection=proj,
+                     learn_dt=learn_dt, bias=bias, elementwise_affine=affine, use_triton=False, vec_dt=vec_dt)
+        with torch.no_grad():  # move every parameter off its init value
+            for prm in layer.parameters():
+                prm.add_(0.3 * torch.randn_like(prm))
+            if proj == "mean":
+                layer.projection_dir.add_(0.2 * torch.randn_like(layer.projection_dir))
+                layer.projection_dir.div_(layer.projection_dir.norm())
+        x = torch.randn(2, 5, inp, requires_grad=True)
+        g = torch.randn(2, 5, inp)
+        y = layer(x)
+        y.backward(g)
+        key = f"c{ci}"
+        rec[f"{key}/meta"] = np.array([n, m, E, gen_codes.index(gen), proj_codes.index(proj), int(vec_dt),
+                                       int(learn_dt), int(bias), int(affine)])
+        rec[f"{key}/x"] = x.detach().numpy()
+        rec[f"{key}/g"] = g.numpy()
+        rec[f"{key}/out"] = y.detach().numpy()
+        rec[f"{key}/grad_x"] = x.grad.numpy()
+        for name, t in layer.state_dict().items():
+            rec[f"{key}/sd/{name}"] = t.detach().numpy()
+        for name, prm in layer.named_parameters():
+            if prm.grad is not None:
+                rec[f"{key}/grad/{name}"] = prm.grad.numpy()
+    np.savez_compressed(os.path.join(out, "module.npz"), **rec)
+
+
 def gen_generator(out):
     """CGHC's generator (cghc.py:219-315) for every generator type, scalar and
     per-stream dt, computed by the reference layer's own compute_generator
@@ -460,18 +516,27 @@ def gen_sinkhorn(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("HC_REFERENCE"),
+                    help="root of a pjjajal/hyperconnections checkout (default: $HC_REFERENCE)")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", nargs="*", help="generate only these fixture groups (function names without gen_)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference or set HC_REFERENCE to the reference checkout")
     ref_expm, ref_small = _import_reference(args.reference)
-    gen_expm(ref_expm, args.out)
-    gen_stream_mix(ref_small, args.out)
-    gen_stream_mix_large_n(ref_small, args.out)
-    gen_fused(ref_small, args.out)
-    gen_rw(ref_small, args.out)
-    gen_layer(args.reference, args.out)
-    gen_sinkhorn(args.out)
-    gen_generator(args.out)
+    groups = {
+        "expm": lambda: gen_expm(ref_expm, args.out),
+        "stream_mix": lambda: gen_stream_mix(ref_small, args.out),
+        "stream_mix_large_n": lambda: gen_stream_mix_large_n(ref_small, args.out),
+        "fused": lambda: gen_fused(ref_small, args.out),
+        "rw": lambda: gen_rw(ref_small, args.out),
+        "layer": lambda: gen_layer(args.reference, args.out),
+        "module": lambda: gen_module(args.out),
+        "sinkhorn": lambda: gen_sinkhorn(args.out),
+        "generator": lambda: gen_generator(args.out),
+    }
+    for name in args.only or groups:
+        groups[name]()
     for name in sorted(os.listdir(args.out)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(args.out, name)), "bytes")
