@@ -11,12 +11,13 @@ The forward runs
     R, W    = sigmoid read / 2 sigmoid write weights          (cghc.py:323-339)
     u       = hc_read(R, x)                        width-read (cghc.py:410)
     f       = module(u)                                        (cghc.py:413)
-    A       = cghc_generator(pre-activations)      one kernel (cghc.py:219-315)
-    Phi     = matrix_exp(A)                        Pade kernel (cghc.py:321)
+    Phi     = cghc_transition(pre-activations)     one kernel: the generator
+                                                   (cghc.py:219-315) fused with
+                                                   the Pade exponential (:321)
     x_new   = hc_mix_write(Phi, x, W, f, v)        depth-write + mix (cghc.py:417, :449)
 
 so the written term Y = W f is never materialised, the generator's tens of
-small elementwise ops are one launch, and the six Linear heads that read the
+small elementwise ops and the exponential are one launch, and the Linear heads that read the
 normalised stream (read, write, two dt heads, generator heads, projection) are
 one GEMM instead of six reads of x_norm.
 
@@ -35,7 +36,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .ops import cghc_generator, hc_mix_write, hc_read, matrix_exp
+from .ops import cghc_transition, hc_mix_write, hc_read
 
 GeneratorType = Literal["conservative", "psd_diss", "diagonal_diss", "laplacian", "conservative_diag_diss",
                         "conservative_psd_diss", "conservative_laplacian"]
@@ -194,7 +195,7 @@ class ContinuousGenHyperConnections(nn.Module):
 
         gt = self.generator_type
         dissipative = gt in _PSD | _DIAG | _LAPLACIAN
-        A = cghc_generator(
+        Phi = cghc_transition(
             M=self.conserv_A + h["conv_pred"].view(T, n, n) if gt in _CONSERV else None,
             logit_conserv=self.log_dt_conserv + h["dtc"] if gt in _CONSERV else None,
             R=self.diss_A + h["diss_pred"].view(T, n, n) if gt in _PSD else None,
@@ -203,7 +204,6 @@ class ContinuousGenHyperConnections(nn.Module):
             logit_diss=self.log_dt_diss + h["dtd"] if dissipative else None,
             dt_range_conserv=(self.dt_min_cons, self.dt_max_cons), dt_range_diss=(self.dt_min_diss, self.dt_max_diss),
             vec_dt=self.vec_dt)
-        Phi = matrix_exp(A)
         if self.projection == "mean":
             v = self.projection_dir.unsqueeze(0)
         elif self.projection == "v":

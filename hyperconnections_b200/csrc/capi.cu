@@ -18,4 +18,4 @@ extern "C" const char* hc_error_string(int code) {
   }
 }
 
-extern "C" int hc_abi_version(void) { return 6; }
+extern "C" int hc_abi_version(void) { return 7; }

@@ -37,6 +37,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "generator.cuh"
 
 namespace hc {
 namespace {
@@ -1010,6 +1011,103 @@ __global__ void __launch_bounds__(kExpmThreads) expm_pade_bwd_kernel(const float
   store_row<N>(dA, mat, batch, r, dt);
 }
 
+// ------------------------------------------------ generator fused with Pade
+// CGHC's transition Phi = exp(A) straight from the module's pre-activations
+// (cghc.py:219-321), for a block of kExpmThreads / G tokens. One thread per
+// token assembles A with the generator's own device code (generator.cuh) into
+// shared memory; then G lanes per token run the Pade [7/7] evaluation on its
+// rows exactly as expm_pade_fwd_kernel does on A read from global memory. The
+// result is bit for bit that of the two launches, without A's round trip
+// through HBM and one launch fewer.
+template <int N, bool VEC>
+__global__ void __launch_bounds__(kExpmThreads) transition_fwd_kernel(const GenArgs a, int flags,
+                                                                      float* __restrict__ E) {
+  constexpr int G = Group<N>::G;
+  constexpr int MPB = kExpmThreads / G;
+  __shared__ float sA[MPB * N * N];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * MPB;
+  if (threadIdx.x < MPB) {
+    const int64_t t = t0 + threadIdx.x;
+    float A[N * N];
+    if (t < a.T) {
+      gen_forward_token<N, VEC>(a, flags, t, A);
+    } else {
+#pragma unroll
+      for (int k = 0; k < N * N; ++k) A[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) sA[threadIdx.x * N * N + k] = A[k];
+  }
+  __syncthreads();
+  const int lm = threadIdx.x / G;
+  const int r = threadIdx.x & (G - 1);
+  const int64_t mat = t0 + lm;
+  const bool ok = mat < a.T && r < N;
+  float row[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) row[j] = ok ? sA[lm * N * N + r * N + j] : 0.f;
+  const int s = scaling_exponent(norm1_rows<N, G>(row), kTheta7);
+  const float sc = pow2_neg(s);
+#pragma unroll
+  for (int j = 0; j < N; ++j) row[j] *= sc;
+  float t[N];
+  pade7_eval<N, G>(row, r, t);
+  square_s<N, G>(t, s);
+  store_row<N>(E, mat, a.T, r, t);
+}
+
+// Backward of the same: A is assembled again (cheaper than storing it), the
+// Pade Frechet backward of expm_pade_bwd_kernel gives dL/dA per row into
+// shared memory, and one thread per token runs the generator's reverse mode
+// on it. a.G is dL/dPhi here.
+template <int N, bool VEC>
+__global__ void __launch_bounds__(kExpmThreads) transition_bwd_kernel(const GenArgs a, int flags) {
+  constexpr int G = Group<N>::G;
+  constexpr int MPB = kExpmThreads / G;
+  __shared__ float sA[MPB * N * N];
+  __shared__ float sD[MPB * N * N];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * MPB;
+  if (threadIdx.x < MPB) {
+    const int64_t t = t0 + threadIdx.x;
+    float A[N * N];
+    if (t < a.T) {
+      gen_forward_token<N, VEC>(a, flags, t, A);
+    } else {
+#pragma unroll
+      for (int k = 0; k < N * N; ++k) A[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) sA[threadIdx.x * N * N + k] = A[k];
+  }
+  __syncthreads();
+  const int lm = threadIdx.x / G;
+  const int r = threadIdx.x & (G - 1);
+  const int64_t mat = t0 + lm;
+  const bool ok = mat < a.T && r < N;
+  float at[N], e[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) at[j] = ok ? sA[lm * N * N + j * N + r] : 0.f;  // row r of A^T
+  load_row<N>(a.G, mat, a.T, r, e);
+  const int s = scaling_exponent(norm1_from_transpose<N, G>(at), kTheta7);
+  const float sc = pow2_neg(s);
+#pragma unroll
+  for (int j = 0; j < N; ++j) { at[j] *= sc; e[j] *= sc; }
+  float t[N], dt[N];
+  pade7_eval_d<N, G>(at, e, r, t, dt);
+  square_s_d<N, G>(t, dt, s);
+  if (ok) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) sD[lm * N * N + r * N + j] = dt[j];
+  }
+  __syncthreads();
+  if (threadIdx.x < MPB && t0 + threadIdx.x < a.T) {
+    float dA[N * N];
+#pragma unroll
+    for (int k = 0; k < N * N; ++k) dA[k] = sD[threadIdx.x * N * N + k];
+    gen_backward_token<N, VEC>(a, flags, t0 + threadIdx.x, dA);
+  }
+}
+
 // ------------------------------------------------------------ host side
 constexpr int kMaxNormParts = 1024;
 
@@ -1269,6 +1367,68 @@ extern "C" int hc_expm_pade_bwd(const float* A, const float* G, float* dA, int64
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid = expm_grid(batch, n);
 #define L(NN) expm_pade_bwd_kernel<NN><<<grid, kExpmThreads, 0, st>>>(A, G, dA, batch)
+  HC_EXPM_SWITCH(n, L)
+#undef L
+  return launch_status();
+}
+
+namespace hc {
+namespace {
+
+int check_transition(const GenArgs& a, int n, int flags) {
+  if (a.T > (int64_t(1) << 34)) return HC_ERR_BAD_SIZE;  // T / 32 tokens per CTA stays below 2^31 CTAs
+  return check_gen(a, n, flags);
+}
+
+unsigned transition_grid(int64_t T, int n) {
+  const int G = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
+  const int64_t per_cta = kExpmThreads / G;
+  return static_cast<unsigned>((T + per_cta - 1) / per_cta);
+}
+
+}  // namespace
+}  // namespace hc
+
+extern "C" int hc_cghc_transition_fwd(const float* M, const float* lc, const float* R, const float* dpre,
+                                      const float* S, const float* ld, float* Phi, int64_t T, int n, int vec_dt,
+                                      int flags, float dt_min_c, float dt_max_c, float dt_min_d, float dt_max_d,
+                                      void* stream) {
+  HC_ENTRY("hc_cghc_transition_fwd");
+  GenArgs a{};
+  a.M = M; a.lc = lc; a.ld = ld; a.R = R; a.dpre = dpre; a.S = S; a.T = T;
+  a.lo_c = dt_min_c; a.hi_c = dt_max_c; a.lo_d = dt_min_d; a.hi_d = dt_max_d;
+  int rc = check_transition(a, n, flags);
+  if (rc || T == 0) return rc;
+  if (!Phi) return HC_ERR_NULL_POINTER;
+  if (!aligned4(Phi)) return HC_ERR_ALIGNMENT;
+  const unsigned grid = transition_grid(T, n);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define L(NN)                                                                                  \
+  if (vec_dt) transition_fwd_kernel<NN, true><<<grid, kExpmThreads, 0, st>>>(a, flags, Phi);  \
+  else transition_fwd_kernel<NN, false><<<grid, kExpmThreads, 0, st>>>(a, flags, Phi)
+  HC_EXPM_SWITCH(n, L)
+#undef L
+  return launch_status();
+}
+
+extern "C" int hc_cghc_transition_bwd(const float* M, const float* lc, const float* R, const float* dpre,
+                                      const float* S, const float* ld, const float* G, float* dM, float* dlc,
+                                      float* dR, float* ddpre, float* dS, float* dld, int64_t T, int n, int vec_dt,
+                                      int flags, float dt_min_c, float dt_max_c, float dt_min_d, float dt_max_d,
+                                      void* stream) {
+  HC_ENTRY("hc_cghc_transition_bwd");
+  GenArgs a{};
+  a.M = M; a.lc = lc; a.ld = ld; a.R = R; a.dpre = dpre; a.S = S; a.G = G; a.T = T;
+  a.dM = dM; a.dlc = dlc; a.dld = dld; a.dR = dR; a.ddpre = ddpre; a.dS = dS;
+  a.lo_c = dt_min_c; a.hi_c = dt_max_c; a.lo_d = dt_min_d; a.hi_d = dt_max_d;
+  int rc = check_transition(a, n, flags);
+  if (rc || T == 0) return rc;
+  if (!G) return HC_ERR_NULL_POINTER;
+  const unsigned grid = transition_grid(T, n);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define L(NN)                                                                           \
+  if (vec_dt) transition_bwd_kernel<NN, true><<<grid, kExpmThreads, 0, st>>>(a, flags);  \
+  else transition_bwd_kernel<NN, false><<<grid, kExpmThreads, 0, st>>>(a, flags)
   HC_EXPM_SWITCH(n, L)
 #undef L
   return launch_status();

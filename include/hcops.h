@@ -202,6 +202,30 @@ int hc_cghc_generator_bwd(const float* M, const float* lc, const float* R,
                           int vec_dt, int flags, float dt_min_c, float dt_max_c,
                           float dt_min_d, float dt_max_d, void* stream);
 
+/* CGHC's transition Phi = exp(A) [T,n,n] straight from the pre-activations
+ * of hc_cghc_generator_fwd (same arguments and flags): the generator and the
+ * Pade [7/7] exponential of hc_expm_pade_fwd in one kernel, bit for bit the
+ * result of the two calls, without A's round trip through memory.
+ * Replaces: hyperconnections/cghc.py:219-321 (compute_generator, then
+ * torch.linalg.matrix_exp in compute_transition). */
+int hc_cghc_transition_fwd(const float* M, const float* lc, const float* R,
+                           const float* dpre, const float* S, const float* ld,
+                           float* Phi, int64_t T, int n, int vec_dt, int flags,
+                           float dt_min_c, float dt_max_c, float dt_min_d,
+                           float dt_max_d, void* stream);
+
+/* Given G = dL/dPhi [T,n,n]: the gradients with respect to each
+ * pre-activation, as hc_cghc_generator_bwd gives them for dL/dA (A is
+ * assembled again inside the kernel; any output may be NULL).
+ * Replaces the autograd backward of cghc.py:219-321. */
+int hc_cghc_transition_bwd(const float* M, const float* lc, const float* R,
+                           const float* dpre, const float* S, const float* ld,
+                           const float* G, float* dM, float* dlc, float* dR,
+                           float* ddpre, float* dS, float* dld, int64_t T,
+                           int n, int vec_dt, int flags, float dt_min_c,
+                           float dt_max_c, float dt_min_d, float dt_max_d,
+                           void* stream);
+
 /* ===========================================================================
  * stream_mix_add: out = Phi x + Y              (v == NULL)
  *                 out = Phi x + (v - Phi v)(v^T x) + Y   (v != NULL)
