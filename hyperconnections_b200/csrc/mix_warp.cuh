@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <cmath>
 #include <type_traits>
+#include <utility>
 
 #include "mix_kernels.cuh"
 
@@ -81,6 +82,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+
+// Programmatic dependent launch. The ring kernels are launched with
+// programmatic stream serialization allowed (launch_ring below). At entry a
+// CTA lets the next kernel of the stream be scheduled (so that kernel's CTAs
+// can take an SM the moment this kernel's CTA on it exits, and set up their
+// rings while the rest of this grid finishes); after its own barrier setup it
+// waits for the previous kernel of the stream to complete and flush before
+// touching global memory. Both instructions are no-ops for a kernel launched
+// without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 constexpr int kRingMaxStages = 32;  // stages of the per-CTA ring
 constexpr int kWarpMaxWarps = 16;   // producer + consumers
@@ -735,7 +749,9 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
   constexpr int es = sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
+  pdl_launch_dependents();
   ring_init(st, geo.stages);
+  pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
@@ -1222,7 +1238,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
   __shared__ RingState st;
   // per-consumer Gram of the blocked path
   __shared__ float gram_all[BLK ? (kWarpMaxWarps - 1) * GramShape<N, FUSED>::SIZE : 1];
+  pdl_launch_dependents();
   ring_init(st, geo.stages);
+  pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
@@ -1428,6 +1446,31 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
   return true;
 }
 
+#ifndef HC_PDL
+#define HC_PDL 1  // build flag: launch the ring kernels with programmatic stream serialization
+#endif
+
+// Launch of a ring kernel (see pdl_launch_dependents).
+template <typename... KArgs, typename... Args>
+inline int launch_ring(void (*kernel)(KArgs...), int grid, dim3 block, int smem_bytes, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = HC_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) != cudaSuccess) {
+    cudaGetLastError();
+    return HC_ERR_LAUNCH;
+  }
+  return HC_OK;
+}
+
 template <typename KernelT>
 inline int warp_prepare(KernelT* kernel, int smem_bytes) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
@@ -1451,7 +1494,7 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, 
   case NN: {                                                            \
     auto* k = mix_fwd_warp_kernel<T, P, NN, FUSED, PROJ, fwd_lane_words(NN)>;       \
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;            \
-    k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);                  \
+    if (int rc = launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo)) return rc; \
     break;                                                              \
   }
     HC_CASE(1) HC_CASE(2) HC_CASE(3) HC_CASE(4) HC_CASE(5) HC_CASE(6) HC_CASE(7) HC_CASE(8)
@@ -1465,8 +1508,7 @@ template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK>
 int launch_bwd_kernel(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
   auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK>;
   if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-  k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);
-  return HC_OK;
+  return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ>

@@ -162,7 +162,9 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   constexpr int NIN = MIXW ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
+  pdl_launch_dependents();
   ring_init(st, geo.stages);
+  pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
@@ -409,7 +411,9 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   constexpr int NIN = MIXW ? 3 : 2;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ RingState st;
+  pdl_launch_dependents();
   ring_init(st, geo.stages);
+  pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
   const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
@@ -642,13 +646,12 @@ int rw_launch_one(const WarpGeometry& geo_in, const RwArgs& a, cudaStream_t s) {
   if constexpr (BWD) {
     auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ>;
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-    k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);
+    return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
   } else {
     auto* k = rw_fwd_warp_kernel<T, N, M, MIXW, PROJ>;
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-    k<<<geo.grid, block, geo.smem_bytes, s>>>(a, geo);
+    return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
   }
-  return launch_status();
 }
 
 template <typename T, bool BWD, bool MIXW, bool PROJ, int N>
