@@ -59,13 +59,15 @@ _SIGNATURES = {
     "hc_sinkhorn_bwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _vp]),
     "hc_cghc_generator_fwd": (_c_int, [_vp] * 7 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
     "hc_cghc_generator_bwd": (_c_int, [_vp] * 13 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
+    "hc_cghc_transition_fwd": (_c_int, [_vp] * 7 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
+    "hc_cghc_transition_bwd": (_c_int, [_vp] * 13 + [_c_i64, _c_int, _c_int, _c_int] + [ctypes.c_float] * 4 + [_vp]),
     "hc_read_fwd": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_read_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_fwd": (_c_int, [_vp] * 6 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
     "hc_mix_write_bwd": (_c_int, [_vp] * 11 + [_c_i64, _c_int, _c_int, _c_i64, _c_int, _vp]),
 }
 
-EXPECTED_ABI_VERSION = 6
+EXPECTED_ABI_VERSION = 7
 
 _lib: Optional[ctypes.CDLL] = None
 _load_error: Optional[str] = None
@@ -126,9 +128,37 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
     """Raw cudaStream_t of torch's current stream on the tensor's device."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class on_device:
+    """Make the tensor's device current for a launch; a no-op (no device
+    switch) when it already is, the common case."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
 
 
 HC_ERR_TIMEOUT = 8

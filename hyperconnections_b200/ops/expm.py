@@ -41,8 +41,31 @@ def _flatten(A: torch.Tensor, name: str):
     n = A.shape[-1]
     if not 1 <= n <= MAX_ORDER:
         raise RuntimeError(f"{name} supports 1 <= n <= {MAX_ORDER}, got n={n}")
-    A32 = A.to(torch.float32).contiguous().view(-1, n, n)
-    return A32, n
+    if A.dtype != torch.float32:
+        A = A.to(torch.float32)
+    if not A.is_contiguous():
+        A = A.contiguous()
+    return A.view(-1, n, n), n
+
+
+_SCRATCH_WORDS: dict = {}
+
+
+def _scratch_words(batch: int, n: int, device_index: int) -> int:
+    """Floats of global-scaling scratch for (batch, n) on a device (depends
+    on the device's occupancy; cached)."""
+    key = (batch, n, device_index)
+    words = _SCRATCH_WORDS.get(key)
+    if words is None:
+        words = max(1, int(_lib.lib().hc_expm_t18_scratch_words(batch, n)))
+        if len(_SCRATCH_WORDS) < 4096:
+            _SCRATCH_WORDS[key] = words
+    return words
+
+
+def _restore(t: torch.Tensor, shape, dtype) -> torch.Tensor:
+    t = t.view(shape)
+    return t if dtype == torch.float32 else t.to(dtype)
 
 
 class _ExpmT18Fn(torch.autograd.Function):
@@ -50,39 +73,42 @@ class _ExpmT18Fn(torch.autograd.Function):
     def forward(ctx, A, per_matrix):
         A32, n = _flatten(A, "expm_t18")
         batch = A32.shape[0]
-        E = torch.empty_like(A32)
-        lib = _lib.lib()
-        words = max(1, lib.hc_expm_t18_scratch_words(batch, n))
-        scratch = None if per_matrix else torch.empty(words, dtype=torch.float32, device=A32.device)
-        with torch.cuda.device(A32.device):
-            rc = lib.hc_expm_t18_fwd(
-                A32.data_ptr(), E.data_ptr(), batch, n, _lib.ptr(scratch), words if scratch is not None else 0,
-                1 if per_matrix else 0, _lib.stream_of(A32),
-            )
+        size = batch * n * n
+        buf = None
+        if per_matrix:
+            E = torch.empty_like(A32)
+            scratch_ptr, words = None, 0
+        else:
+            # one allocation: E, then the partial maxima the backward reuses
+            words = _scratch_words(batch, n, A32.device.index)
+            buf = torch.empty(size + words, dtype=torch.float32, device=A32.device)
+            E = buf[:size].view(batch, n, n)
+            scratch_ptr = buf.data_ptr() + 4 * size
+        with _lib.on_device(A32):
+            rc = _lib.lib().hc_expm_t18_fwd(A32.data_ptr(), E.data_ptr(), batch, n, scratch_ptr, words,
+                                            1 if per_matrix else 0, _lib.stream_of(A32))
         _lib.check(rc, "hc_expm_t18_fwd")
         ctx.save_for_backward(A32)
-        ctx.scratch = scratch  # the partial maxima of A, reused by the backward
+        ctx.keep = buf  # holds the partial maxima the backward reuses
+        ctx.scratch = (scratch_ptr, words)
         ctx.per_matrix = per_matrix
         ctx.shape = A.shape
         ctx.dtype = A.dtype
-        return E.view(A.shape).to(A.dtype)
+        return _restore(E, A.shape, A.dtype)
 
     @staticmethod
     def backward(ctx, grad):
         (A32,) = ctx.saved_tensors
         batch, n, _ = A32.shape
-        G = grad.to(torch.float32).contiguous().view(batch, n, n)
+        G = grad if grad.dtype == torch.float32 else grad.to(torch.float32)
+        G = (G if G.is_contiguous() else G.contiguous()).view(batch, n, n)
         dA = torch.empty_like(A32)
-        lib = _lib.lib()
-        scratch = ctx.scratch
-        words = 0 if scratch is None else scratch.numel()
-        with torch.cuda.device(A32.device):
-            rc = lib.hc_expm_t18_bwd(
-                A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n, _lib.ptr(scratch), words,
-                1 if ctx.per_matrix else 2, _lib.stream_of(A32),
-            )
+        scratch_ptr, words = ctx.scratch
+        with _lib.on_device(A32):
+            rc = _lib.lib().hc_expm_t18_bwd(A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n, scratch_ptr,
+                                            words, 1 if ctx.per_matrix else 2, _lib.stream_of(A32))
         _lib.check(rc, "hc_expm_t18_bwd")
-        return dA.view(ctx.shape).to(ctx.dtype), None
+        return _restore(dA, ctx.shape, ctx.dtype), None
 
 
 class _ExpmPadeFn(torch.autograd.Function):
@@ -91,26 +117,26 @@ class _ExpmPadeFn(torch.autograd.Function):
         A32, n = _flatten(A, "matrix_exp")
         batch = A32.shape[0]
         E = torch.empty_like(A32)
-        lib = _lib.lib()
-        with torch.cuda.device(A32.device):
-            rc = lib.hc_expm_pade_fwd(A32.data_ptr(), E.data_ptr(), batch, n, _lib.stream_of(A32))
+        with _lib.on_device(A32):
+            rc = _lib.lib().hc_expm_pade_fwd(A32.data_ptr(), E.data_ptr(), batch, n, _lib.stream_of(A32))
         _lib.check(rc, "hc_expm_pade_fwd")
         ctx.save_for_backward(A32)
         ctx.shape = A.shape
         ctx.dtype = A.dtype
-        return E.view(A.shape).to(A.dtype)
+        return _restore(E, A.shape, A.dtype)
 
     @staticmethod
     def backward(ctx, grad):
         (A32,) = ctx.saved_tensors
         batch, n, _ = A32.shape
-        G = grad.to(torch.float32).contiguous().view(batch, n, n)
+        G = grad if grad.dtype == torch.float32 else grad.to(torch.float32)
+        G = (G if G.is_contiguous() else G.contiguous()).view(batch, n, n)
         dA = torch.empty_like(A32)
-        lib = _lib.lib()
-        with torch.cuda.device(A32.device):
-            rc = lib.hc_expm_pade_bwd(A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n, _lib.stream_of(A32))
+        with _lib.on_device(A32):
+            rc = _lib.lib().hc_expm_pade_bwd(A32.data_ptr(), G.data_ptr(), dA.data_ptr(), batch, n,
+                                             _lib.stream_of(A32))
         _lib.check(rc, "hc_expm_pade_bwd")
-        return dA.view(ctx.shape).to(ctx.dtype)
+        return _restore(dA, ctx.shape, ctx.dtype)
 
 
 def expm_t18(A: torch.Tensor, per_matrix_scaling: bool = False) -> torch.Tensor:

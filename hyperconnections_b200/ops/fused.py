@@ -38,7 +38,7 @@ class _FusedFn(torch.autograd.Function):
         u = torch.empty(T, D, dtype=x.dtype, device=x.device)
         x_out = torch.empty_like(x_c)
         lib = _lib.lib()
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x_c):
             rc = lib.hc_fused_fwd(
                 x_c.data_ptr(), f_c.data_ptr(), H_c.data_ptr(), a_c.data_ptr(), b_c.data_ptr(),
                 u.data_ptr(), x_out.data_ptr(), T, n, D, _lib.dtype_code(x.dtype), _lib.stream_of(x_c),
@@ -64,7 +64,7 @@ class _FusedFn(torch.autograd.Function):
         grad_a = torch.empty(T, n, dtype=torch.float32, device=dev) if need_a else None
         grad_b = torch.empty(T, n, dtype=torch.float32, device=dev) if need_b else None
         lib = _lib.lib()
-        with torch.cuda.device(dev):
+        with _lib.on_device(x_c):
             rc = lib.hc_fused_bwd(
                 g_u.data_ptr(), g_x.data_ptr(), x_c.data_ptr(), f_c.data_ptr(), H_c.data_ptr(),
                 a_c.data_ptr(), b_c.data_ptr(), _lib.ptr(grad_x), _lib.ptr(grad_f), _lib.ptr(grad_H),

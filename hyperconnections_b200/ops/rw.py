@@ -53,7 +53,7 @@ class _ReadFn(torch.autograd.Function):
         x_c = x.contiguous().view(T, n, D)
         R_c = _f32(R, (T, m, n))
         u = torch.empty(T, m, D, dtype=x.dtype, device=x.device)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x_c):
             rc = _lib.lib().hc_read_fwd(R_c.data_ptr(), x_c.data_ptr(), u.data_ptr(), T, n, m, D,
                                         _lib.dtype_code(x.dtype), _lib.stream_of(x_c))
         _lib.check(rc, "hc_read_fwd")
@@ -71,7 +71,7 @@ class _ReadFn(torch.autograd.Function):
         g = g_u.to(dt).contiguous().view(T, m, D)
         grad_x = torch.empty_like(x_c) if need_x else None
         grad_R = torch.empty(T, m, n, dtype=torch.float32, device=dev) if need_R else None
-        with torch.cuda.device(dev):
+        with _lib.on_device(x_c):
             rc = _lib.lib().hc_read_bwd(g.data_ptr(), R_c.data_ptr(), x_c.data_ptr(), _lib.ptr(grad_x),
                                         _lib.ptr(grad_R), T, n, m, D, _lib.dtype_code(dt), _lib.stream_of(x_c))
         _lib.check(rc, "hc_read_bwd")
@@ -93,7 +93,7 @@ class _MixWriteFn(torch.autograd.Function):
         W_c = _f32(W, (T, n, m))
         v_c = None if v is None else _f32(v.expand(*lead, n), (T, n))
         out = torch.empty_like(x_c)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x_c):
             rc = _lib.lib().hc_mix_write_fwd(H_c.data_ptr(), x_c.data_ptr(), W_c.data_ptr(), f_c.data_ptr(),
                                              _lib.ptr(v_c), out.data_ptr(), T, n, m, D,
                                              _lib.dtype_code(x.dtype), _lib.stream_of(x_c))
@@ -118,7 +118,7 @@ class _MixWriteFn(torch.autograd.Function):
         grad_H = torch.empty(T, n, n, dtype=torch.float32, device=dev) if need_H else None
         grad_W = torch.empty(T, n, m, dtype=torch.float32, device=dev) if need_W else None
         grad_v = torch.empty(T, n, dtype=torch.float32, device=dev) if need_v else None
-        with torch.cuda.device(dev):
+        with _lib.on_device(x_c):
             rc = _lib.lib().hc_mix_write_bwd(
                 g_c.data_ptr(), H_c.data_ptr(), x_c.data_ptr(), W_c.data_ptr(), f_c.data_ptr(), _lib.ptr(v_c),
                 _lib.ptr(grad_x), _lib.ptr(grad_f), _lib.ptr(grad_H), _lib.ptr(grad_W), _lib.ptr(grad_v),

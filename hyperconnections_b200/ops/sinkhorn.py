@@ -27,7 +27,7 @@ class _SinkhornFn(torch.autograd.Function):
         H32 = H.to(torch.float32).contiguous().view(-1, n, n)
         P = torch.empty_like(H32)
         batch = H32.shape[0]
-        with torch.cuda.device(H.device):
+        with _lib.on_device(H):
             rc = _lib.lib().hc_sinkhorn_fwd(H32.data_ptr(), P.data_ptr(), batch, n, iters, _lib.stream_of(H32))
         _lib.check(rc, "hc_sinkhorn_fwd")
         ctx.save_for_backward(H32)
@@ -40,7 +40,7 @@ class _SinkhornFn(torch.autograd.Function):
         batch, n, _ = H32.shape
         G = grad.to(torch.float32).contiguous().view(batch, n, n)
         dH = torch.empty_like(H32)
-        with torch.cuda.device(H32.device):
+        with _lib.on_device(H32):
             rc = _lib.lib().hc_sinkhorn_bwd(H32.data_ptr(), G.data_ptr(), dH.data_ptr(), batch, n, ctx.iters,
                                             _lib.stream_of(H32))
         _lib.check(rc, "hc_sinkhorn_bwd")

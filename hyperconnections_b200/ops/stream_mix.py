@@ -54,7 +54,7 @@ class _StreamMixFn(torch.autograd.Function):
         B, N, D = x_c.shape
         out = torch.empty_like(x_c)
         lib = _lib.lib()
-        with torch.cuda.device(x_c.device):
+        with _lib.on_device(x_c):
             rc = lib.hc_stream_mix_fwd(
                 Phi_c.data_ptr(), x_c.data_ptr(), Y_c.data_ptr(), _lib.ptr(v_c), out.data_ptr(),
                 B, N, D, _lib.dtype_code(x_c.dtype), _lib.dtype_code(pdt), _lib.stream_of(x_c),
@@ -77,7 +77,7 @@ class _StreamMixFn(torch.autograd.Function):
         grad_v = torch.empty(B, N, dtype=torch.float32, device=x_c.device) if need_v else None
         if need_x or need_phi or need_v:
             lib = _lib.lib()
-            with torch.cuda.device(x_c.device):
+            with _lib.on_device(x_c):
                 rc = lib.hc_stream_mix_bwd(
                     G.data_ptr(), Phi_c.data_ptr(), x_c.data_ptr(), _lib.ptr(v_c),
                     _lib.ptr(grad_x), _lib.ptr(grad_phi), _lib.ptr(grad_v),
