@@ -215,12 +215,17 @@ class FusedRunner:
     """Direct C-ABI launches of the fused forward and backward on resident
     device buffers (the kernels timed for ``value``)."""
 
-    def __init__(self, device, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0):
+    def __init__(self, device, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0, shard=None):
         from hyperconnections_b200 import _lib
 
         self.lib = _lib.lib()
-        self.T, self.n, self.D = T, n, D
         host = fused_workload(T, n, D, seed=seed)
+        if shard is not None:  # (rank, world): this rank's contiguous slice of the seeded batch
+            rank, world = shard
+            lo, hi = T * rank // world, T * (rank + 1) // world
+            host = [t[lo:hi].contiguous() for t in host]
+            T = hi - lo
+        self.T, self.n, self.D = T, n, D
         self.x, self.f, self.H, self.alpha, self.beta, self.g_u, self.g_x = [t.to(device) for t in host]
         dt = self.x.dtype
         self.u = torch.empty(T, D, dtype=dt, device=device)
@@ -250,10 +255,15 @@ class FusedRunner:
         self._check(rc, "hc_fused_bwd")
 
 
-def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0):
-    runner = FusedRunner(device, T=T, n=n, D=D, seed=seed)
+def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0, shard=None):
+    """Two timed passes of `steps` fused steps each, L2 flushed before every
+    step outside the events. Pass 1 records events only around the step
+    (forward then backward back to back, as a training step runs them: the
+    backward's CTAs may start on SMs the forward has left, programmatic
+    dependent launch); its times are the headline. Pass 2 adds an event between
+    the kernels for the per-kernel split and the dominant kernel's roofline."""
+    runner = FusedRunner(device, T=T, n=n, D=D, seed=seed, shard=shard)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for _ in range(warmup):
         flush.fill_(1.0)
         runner.fwd()
@@ -262,8 +272,20 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
     barrier(world)
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
+    steps_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
     for i in range(steps):
         flush.fill_(float(i))  # evict L2 between steps, outside the events
+        e = steps_ev[i]
+        e[0].record()
+        runner.fwd()
+        runner.bwd()
+        e[1].record()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    t1 = time.perf_counter()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(float(i))
         e = evs[i]
         e[0].record()
         runner.fwd()
@@ -271,12 +293,11 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
         runner.bwd()
         e[2].record()
     torch.cuda.synchronize(device)
-    barrier(world)
-    t1 = time.perf_counter()
+    step_ms = [e[0].elapsed_time(e[1]) for e in steps_ev]
     fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
     bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
     del flush
-    return {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t1), "launches": 2 * steps}
+    return {"step_ms": step_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t1), "launches": 2 * steps}
 
 
 class ExpmRunner:
@@ -596,11 +617,19 @@ def run_b200(args):
 
     fwd_ms = float(np.mean(res["fwd_ms"]))
     bwd_ms = float(np.mean(res["bwd_ms"]))
-    step_ms = fwd_ms + bwd_ms
+    step_ms = float(np.mean(res["step_ms"]))
     step_ms_max = max_over_ranks(step_ms, world, device)
     rank_ms = gather_ranks(step_ms, world, device)
     fb, bb = fused_bytes(TOKENS, N_STREAMS, BLOCK)
     value = world * (fb + bb) / (step_ms_max * 1e-3) / 1e9
+
+    # the same step with the global batch fixed: rank r keeps its contiguous 1/N slice of the seed-0 batch
+    if world > 1:
+        strong = time_fused(device, args.steps, args.warmup, world, seed=0, shard=(rank, world))
+        strong_ms = max_over_ranks(float(np.mean(strong["step_ms"])), world, device)
+    else:
+        strong_ms = step_ms_max
+    strong_value = (fb + bb) / (strong_ms * 1e-3) / 1e9
 
     expm_ms, expm_fwd_ms = time_expm(device, max(5, min(args.steps, 50)), max(3, args.warmup), split=True)
     expm_step = float(np.mean(expm_ms))
@@ -644,8 +673,13 @@ def run_b200(args):
             "config": CONFIG,
             "pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
             "pct_of_measured_hbm": 100.0 * value / world / peak,
-            "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms},
+            "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms,
+                           "note": "separate pass with an event between the kernels"},
             "rank_ms_per_step": rank_ms,
+            "strong_scaling": {"value": strong_value, "unit": "GB/s", "ms_per_step": strong_ms,
+                               "tokens_per_rank": TOKENS // world,
+                               "what": "the same step with the 16,384-token batch split over the ranks "
+                                       "(rank r keeps its contiguous 1/N slice of the seed-0 batch)"},
             "roofline": {
                 "bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
@@ -943,9 +977,10 @@ def run_sweep(args):
             res = time_fused(device, steps, args.warmup, 1, T=TOKENS, n=n, D=D)
             fwd_ms, bwd_ms = float(np.mean(res["fwd_ms"])), float(np.mean(res["bwd_ms"]))
             fb, bb = fused_bytes(TOKENS, n, D)
-            gbs = (fb + bb) / ((fwd_ms + bwd_ms) * 1e-3) / 1e9
+            gbs = (fb + bb) / (float(np.mean(res["step_ms"])) * 1e-3) / 1e9
             print(json.dumps({
-                "sweep": "fused", "tokens": TOKENS, "n": n, "D": D, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                "sweep": "fused", "tokens": TOKENS, "n": n, "D": D, "step_ms": float(np.mean(res["step_ms"])),
+                "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                 "fwd_gbs": fb / (fwd_ms * 1e-3) / 1e9, "bwd_gbs": bb / (bwd_ms * 1e-3) / 1e9, "gbs": gbs,
                 "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": peak_kind,
                 "pct_of_8tbs": 100.0 * gbs / NOMINAL_HBM_GBS, "bytes": fb + bb}), flush=True)

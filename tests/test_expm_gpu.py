@@ -249,3 +249,26 @@ def test_t18_unaligned_buffers_take_the_scalar_path_bitwise(n):
     for got, want in zip(run(Ao, Go), run(A, G)):
         assert torch.equal(got, want)
     assert _lib.wait_timeouts(reset=True) == 0
+
+
+@pytest.mark.parametrize("n", [2, 4, 6])
+@pytest.mark.parametrize("B", [1000, 65536])
+def test_global_scaling_nan_matrix_poisons_only_itself(n, B):
+    """Deliberate difference from the reference: there one NaN matrix makes
+    the batch maximum of ||A||_1 NaN (ops/expm.py:81-85), hence the scaling
+    exponent and every output of the batch. Here the batch maximum skips NaN
+    norms: the NaN matrix's own output (and gradient) is NaN, every other
+    matrix gets exactly the result it gets when that matrix is zero instead
+    (a zero norm never raises the maximum)."""
+    A, G = config_inputs(B, n, seed=11)
+    k = B // 3
+    A_nan, A_zero = A.clone(), A.clone()
+    A_nan[k] = float("nan")
+    A_zero[k] = 0.0
+    E_nan, dA_nan = fwd_bwd(ops().expm_t18, A_nan, G)
+    E_zero, dA_zero = fwd_bwd(ops().expm_t18, A_zero, G)
+    assert np.isnan(E_nan[k]).all() and np.isnan(dA_nan[k]).all()
+    others = np.ones(B, dtype=bool)
+    others[k] = False
+    assert np.array_equal(E_nan[others], E_zero[others])
+    assert np.array_equal(dA_nan[others], dA_zero[others])
