@@ -623,6 +623,18 @@ def run_b200(args):
     fb, bb = fused_bytes(TOKENS, N_STREAMS, BLOCK)
     value = world * (fb + bb) / (step_ms_max * 1e-3) / 1e9
 
+    if args.fused_only:  # the headline step alone (profiling captures, quick comparisons)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                              "warmup": args.warmup, "ms_per_step": step_ms_max, "fused_only": True,
+                              "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms},
+                              "rank_ms_per_step": rank_ms, "clocks": clocks}), flush=True)
+        sampler.stop()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
+
     # the same step with the global batch fixed: rank r keeps its contiguous 1/N slice of the seed-0 batch
     if world > 1:
         strong = time_fused(device, args.steps, args.warmup, world, seed=0, shard=(rank, world))
@@ -1029,6 +1041,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-models", action="store_true", help="skip the end-to-end ViT / LM training legs")
+    ap.add_argument("--fused-only", action="store_true",
+                    help="time the headline fused step alone and print a short line (profiling, comparisons)")
     ap.add_argument("--sweep", action="store_true", help="print the n x D sweep (16,384 tokens) instead")
     args = ap.parse_args()
     if args.warmup < 3:

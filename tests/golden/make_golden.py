@@ -421,6 +421,57 @@ def gen_module(out):
     np.savez_compressed(os.path.join(out, "module.npz"), **rec)
 
 
+def _record_layer(rec, key, layer, inp, seed, meta):
+    """One layer's state_dict, input, output, upstream gradient and the
+    gradients of the input and every parameter that gets one."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, 5, inp, generator=g).requires_grad_(True)
+    up = torch.randn(2, 5, inp, generator=g)
+    y = layer(x)
+    y.backward(up)
+    rec[f"{key}/meta"] = np.array(meta)
+    rec[f"{key}/x"] = x.detach().numpy()
+    rec[f"{key}/g"] = up.numpy()
+    rec[f"{key}/out"] = y.detach().numpy()
+    rec[f"{key}/grad_x"] = x.grad.numpy()
+    for name, t in layer.state_dict().items():
+        rec[f"{key}/sd/{name}"] = t.detach().numpy()
+    for name, prm in layer.named_parameters():
+        if prm.grad is not None:
+            rec[f"{key}/grad/{name}"] = prm.grad.numpy()
+
+
+def gen_module_ghc_mhc(out):
+    """Whole GHC (hyperconnections/ghc.py:14-128) and MHC (mhc.py:21-150)
+    layers of the reference, float32, wrapping a Linear, with every parameter
+    moved off its init value: the same record as gen_module ("g<i>/...",
+    "m<i>/..."; meta = n, m, embed_dim, bias, affine[, sinkhorn iters])."""
+    from hyperconnections.ghc import GeneralizedHyperConnections as GHC
+    from hyperconnections.mhc import ManifoldHyperConnections as MHC
+
+    rec = {}
+    ghc_cfgs = [(4, 1, 64, False, False), (4, 2, 128, True, False), (6, 3, 96, False, True), (2, 2, 32, False, False),
+                (8, 4, 128, True, True)]
+    for ci, (n, m, E, bias, affine) in enumerate(ghc_cfgs):
+        torch.manual_seed(6000 + ci)
+        layer = GHC(n, m, n * E // m, E, torch.nn.Linear(E, E), bias=bias, elementwise_affine=affine)
+        with torch.no_grad():
+            for prm in layer.parameters():
+                prm.add_(0.3 * torch.randn_like(prm))
+        _record_layer(rec, f"g{ci}", layer, n * E // m, 6100 + ci, [n, m, E, int(bias), int(affine)])
+    mhc_cfgs = [(4, 1, 64, False, False, 20), (4, 2, 128, True, False, 20), (6, 3, 96, False, True, 7),
+                (2, 1, 32, False, False, 0), (8, 4, 128, True, True, 20)]
+    for ci, (n, m, E, bias, affine, iters) in enumerate(mhc_cfgs):
+        torch.manual_seed(7000 + ci)
+        layer = MHC(n, m, n * E // m, E, torch.nn.Linear(E, E), bias=bias, elementwise_affine=affine,
+                    sinkhorn_iters=iters)
+        with torch.no_grad():
+            for prm in layer.parameters():
+                prm.add_(0.3 * torch.randn_like(prm))
+        _record_layer(rec, f"m{ci}", layer, n * E // m, 7100 + ci, [n, m, E, int(bias), int(affine), iters])
+    np.savez_compressed(os.path.join(out, "module_ghc_mhc.npz"), **rec)
+
+
 def gen_generator(out):
     """CGHC's generator (cghc.py:219-315) for every generator type, scalar and
     per-stream dt, computed by the reference layer's own compute_generator
@@ -532,6 +583,7 @@ def main():
         "rw": lambda: gen_rw(ref_small, args.out),
         "layer": lambda: gen_layer(args.reference, args.out),
         "module": lambda: gen_module(args.out),
+        "module_ghc_mhc": lambda: gen_module_ghc_mhc(args.out),
         "sinkhorn": lambda: gen_sinkhorn(args.out),
         "generator": lambda: gen_generator(args.out),
     }
