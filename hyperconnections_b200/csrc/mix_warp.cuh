@@ -1378,7 +1378,15 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   int64_t sl = D;
   int tpi = 1;
   if (tok_bytes > max_stage) {
-    sl = std::max<int64_t>(64, ((16 * 1024) / (rows * esize)) / 64 * 64);
+    if (tune.stage_bytes > 0) {
+      // tuned: the fewest slices of at most the target each, split evenly
+      // (multiples of 64 elements)
+      const int64_t target = std::min<int64_t>(tune.stage_bytes, max_stage);
+      const int64_t ns = (tok_bytes + target - 1) / target;
+      sl = ((D + ns - 1) / ns + 63) / 64 * 64;
+    } else {
+      sl = std::max<int64_t>(64, ((16 * 1024) / (rows * esize)) / 64 * 64);
+    }
     if (sl >= D) sl = D;
   } else if (tok_bytes < item_target) {
     tpi = static_cast<int>(std::min<int64_t>(8, item_target / tok_bytes));
