@@ -96,6 +96,26 @@ def _load() -> Optional[ctypes.CDLL]:
     return _lib
 
 
+_ext = None
+
+
+def torch_ext():
+    """The C++ autograd ops over this library (_hcops_torch.so, built beside
+    it by the same Makefile); raises RuntimeError when it is missing."""
+    global _ext
+    if _ext is None:
+        lib()  # the extension links libhcops.so: load (and version-check) it first
+        try:
+            from . import _hcops_torch as ext
+        except ImportError as exc:
+            raise RuntimeError(f"hyperconnections_b200 torch ops unavailable: {exc} "
+                               "(run `make -C hyperconnections_b200/csrc`)") from None
+        if ext.abi_version() != EXPECTED_ABI_VERSION:
+            raise RuntimeError("_hcops_torch.so was built against another libhcops.so ABI; rebuild it")
+        _ext = ext
+    return _ext
+
+
 def available() -> bool:
     """True when libhcops.so is present and loadable."""
     return _load() is not None
