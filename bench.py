@@ -610,6 +610,20 @@ def run_b200(args):
 
     sampler = ClockSampler(local)
     sampler.start()
+    if args.fused_only and (args.n, args.block) != (N_STREAMS, BLOCK):
+        # another point of the n x D grid, 16,384 tokens (profiling captures)
+        res = time_fused(device, args.steps, args.warmup, world, n=args.n, D=args.block, seed=dist_env()[1])
+        fb, bb = fused_bytes(TOKENS, args.n, args.block)
+        t0, t1 = res["wall"]
+        if rank == 0:
+            step = float(np.mean(res["step_ms"]))
+            print(json.dumps({"fused_only": True, "tokens": TOKENS, "n": args.n, "D": args.block, "ms_per_step": step,
+                              "value": (fb + bb) / (step * 1e-3) / 1e9, "unit": "GB/s",
+                              "kernels_ms": {"hc_fused_fwd": float(np.mean(res["fwd_ms"])),
+                                             "hc_fused_bwd": float(np.mean(res["bwd_ms"]))},
+                              "clocks": sampler.window(t0, t1)}), flush=True)
+        sampler.stop()
+        return
     # rank r's shard: its own seeded batch of the workload (seed r)
     res = time_fused(device, args.steps, args.warmup, world, seed=dist_env()[1])
     t0, t1 = res["wall"]
@@ -1043,6 +1057,8 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the end-to-end ViT / LM training legs")
     ap.add_argument("--fused-only", action="store_true",
                     help="time the headline fused step alone and print a short line (profiling, comparisons)")
+    ap.add_argument("--n", type=int, default=N_STREAMS, help="with --fused-only: streams (16,384 tokens)")
+    ap.add_argument("--block", type=int, default=BLOCK, help="with --fused-only: block size D")
     ap.add_argument("--sweep", action="store_true", help="print the n x D sweep (16,384 tokens) instead")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -243,7 +243,6 @@ struct RingState {
   uint32_t last_parity[kRingMaxStages];
   int issued[kRingMaxStages];
   volatile int abort;
-  uint4 zrow;  // 16 zero bytes: the padding rows of the tensor-core Gram
 };
 
 __device__ __forceinline__ void ring_init(RingState& st, int stages) {
@@ -256,7 +255,6 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
       st.last_parity[s] = 0;
     }
     st.abort = 0;
-    st.zrow = make_uint4(0u, 0u, 0u, 0u);
     fence_mbar_init();
   }
   __syncthreads();
@@ -1020,6 +1018,10 @@ struct GramShape {
 
 // Pass A: grad_x_j = sum_i Phi_ij g_i (+ v_j c^T g) (+ alpha_j g_u) and
 // grad_f = beta^T g over one slice; same arithmetic as bwd_slice.
+#ifndef HC_PASSA_PAIRS
+#define HC_PASSA_PAIRS 1  // build flag: 0 runs pass A's grad_x as scalar FMA chains (measurements)
+#endif
+
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
                                                 const uint8_t* gsb, const uint8_t* usb, int pitch, int64_t t,
@@ -1056,8 +1058,41 @@ __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokPa
           bt[e] = s;
         }
       }
+      // grad_x on packed pairs of output rows (j, j + 1): fma.rn.f32x2 of the
+      // pair (Phi_ij, Phi_i,j+1) with g_i duplicated, two fp32 FMAs per
+      // instruction with each output seeing the same terms in the same order
+      // as one FMA chain; an odd last row runs alone.
+      constexpr int JP = HC_PASSA_PAIRS ? N / 2 : 0;
+      float2 op[JP > 0 ? JP : 1][K];
 #pragma unroll
-      for (int j = 0; j < N; ++j) {
+      for (int e = 0; e < K; ++e) {
+        float2 gg[N];
+#pragma unroll
+        for (int i2 = 0; i2 < N; ++i2) gg[i2] = dup2(ge[i2][e]);
+#pragma unroll
+        for (int k = 0; k < JP; ++k) {
+          float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int i2 = 0; i2 < N; ++i2)
+            s2 = __ffma2_rn(make_float2(pr.phi[i2 * N + 2 * k], pr.phi[i2 * N + 2 * k + 1]), gg[i2], s2);
+          if constexpr (PROJ) s2 = __ffma2_rn(make_float2(pr.vv[2 * k], pr.vv[2 * k + 1]), dup2(bt[e]), s2);
+          if constexpr (FUSED) s2 = __ffma2_rn(make_float2(pr.al[2 * k], pr.al[2 * k + 1]), dup2(gue[e]), s2);
+          op[k][e] = s2;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < JP; ++k) {
+        float lo[K], hi[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          lo[e] = op[k][e].x;
+          hi[e] = op[k][e].y;
+        }
+        gxo[2 * k][w] = Wd::put(lo);
+        gxo[2 * k + 1][w] = Wd::put(hi);
+      }
+#pragma unroll
+      for (int j = 2 * JP; j < N; ++j) {
         float o[K];
 #pragma unroll
         for (int e = 0; e < K; ++e) {
@@ -1147,117 +1182,6 @@ __device__ __forceinline__ void bwd_gram_block(float* gram, const uint8_t* gsb, 
   }
   warp_transpose_reduce<1>(acc, lane);  // lane l: the warp's sum of entry l
   if (lane < RB * NA) gram[R0 * NA + lane] += acc[0];
-}
-
-// ------------------------------------- pass B on the tensor cores (bf16 / fp16)
-// For half-precision streams the slice's Gram M = A B^T (A = [g; g_u] rows, B
-// = [x; f] rows, K = the slice's elements) is a warp-level contraction:
-// ldmatrix loads the rows straight from the ring stage and
-// mma.sync.m16n8k16 (fp32 accumulation; a product of two bf16 / fp16 values is
-// exact in fp32) accumulates a 16 x 8 tile per call, one or two tiles for
-// NA <= 8 or 9 columns. Rows and columns past NA, and the second half of a
-// 16-element step past the slice's end (slices are multiples of 8 elements),
-// read a zeroed 16-byte row. The accumulators stay in registers over all
-// slices of the token; at its last slice they are written to the warp's Gram.
-template <typename T> struct MmaKind;
-template <> struct MmaKind<__nv_bfloat16> {
-  __device__ static __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  }
-};
-template <> struct MmaKind<__half> {
-  __device__ static __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  }
-};
-#ifndef HC_GRAM_MMA
-#define HC_GRAM_MMA 1  // build flag: 0 keeps pass B on the FMA pipe for every dtype (measurements)
-#endif
-template <typename T> constexpr bool gram_on_tensor_cores() { return HC_GRAM_MMA && sizeof(T) == 2; }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-
-template <int N, bool FUSED>
-struct GramMma {
-  static constexpr int NA = N + (FUSED ? 1 : 0);
-  static constexpr int NT = (NA + 7) / 8;  // n8 tiles of columns
-};
-
-// Accumulates one slice of the token's Gram into c (see above). gsb, xsb,
-// usb, fsb: the stage's g, x, g_u and f rows; zrow: 16 zero bytes in shared
-// memory.
-template <typename T, int N, bool FUSED>
-__device__ __forceinline__ void bwd_gram_mma_slice(float (&c)[GramMma<N, FUSED>::NT][4], const uint8_t* gsb,
-                                                   const uint8_t* xsb, const uint8_t* usb, const uint8_t* fsb,
-                                                   const uint8_t* zrow, int pitch, int len, int lane) {
-  constexpr int NA = GramMma<N, FUSED>::NA;
-  constexpr int NT = GramMma<N, FUSED>::NT;
-  constexpr int es = sizeof(T);
-  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
-  const int q = lane >> 3;
-  // A: matrix q holds rows (q & 1) * 8 + (lane & 7), elements (q >> 1) * 8 + [0, 8)
-  const int ar = (q & 1) * 8 + (lane & 7);
-  const uint8_t* arow = ar < N ? gsb + ar * rowb : (FUSED && ar == N ? usb : nullptr);
-  const int akof = (q >> 1) * 8;
-  // B: matrix q holds rows (columns of M) (q >> 1) * 8 + (lane & 7), elements (q & 1) * 8 + [0, 8)
-  const int bj = (q >> 1) * 8 + (lane & 7);
-  const uint8_t* brow = bj < N ? xsb + bj * rowb : (FUSED && bj == N ? fsb : nullptr);
-  const int bkof = (q & 1) * 8;
-  const uint32_t z = smem_u32(zrow);
-  for (int k0 = 0; k0 < len; k0 += 16) {
-    const uint32_t aaddr = (arow && k0 + akof < len) ? smem_u32(arow + (k0 + akof) * es) : z;
-    const uint32_t baddr = (brow && k0 + bkof < len) ? smem_u32(brow + (k0 + bkof) * es) : z;
-    uint32_t af[4];
-    ldsm_x4(af, aaddr);
-    if constexpr (NT == 2) {
-      uint32_t bf[4];
-      ldsm_x4(bf, baddr);
-      MmaKind<T>::mma(c[0], af, bf[0], bf[1]);
-      MmaKind<T>::mma(c[NT - 1], af, bf[2], bf[3]);
-    } else {
-      uint32_t b0, b1;
-      ldsm_x2(b0, b1, baddr);  // lanes 0-15 give the addresses
-      MmaKind<T>::mma(c[0], af, b0, b1);
-    }
-  }
-  (void)NA;
-}
-
-// The token's Gram from the accumulators into the warp's Gram (row-major
-// NA x NA); c[t][0..1] hold row lane / 4, c[t][2..3] row lane / 4 + 8, at
-// columns 8 t + 2 (lane % 4) + {0, 1}.
-template <int N, bool FUSED>
-__device__ __forceinline__ void bwd_gram_mma_store(float* gram, const float (&c)[GramMma<N, FUSED>::NT][4],
-                                                   int lane) {
-  constexpr int NA = GramMma<N, FUSED>::NA;
-  constexpr int NT = GramMma<N, FUSED>::NT;
-  const int r = lane >> 2;
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    const int col = 8 * t + 2 * (lane & 3);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = r + 8 * h;
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-        if (row < NA && col + e < NA) gram[row * NA + col + e] = c[t][2 * h + e];
-    }
-  }
 }
 
 template <typename T, int N, bool FUSED, int W, int R0>
@@ -1386,11 +1310,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
     const int c = warp - 1;
     constexpr bool PAIRS = use_pairs(N);
     constexpr bool BLOCKED = BLK;
-    constexpr bool MMA = BLOCKED && gram_on_tensor_cores<T>();
     using Params = std::conditional_t<PAIRS, TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
     Params pr;
     float acc[BLOCKED ? 1 : L::kPad];
-    float cg[MMA ? GramMma<N, FUSED>::NT : 1][4];  // tensor-core Gram accumulators of the token
     float2 acc2[PAIRS ? L::kAcc : 1];
     float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
     if constexpr (BLOCKED) {
@@ -1425,10 +1347,6 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
 #pragma unroll
               for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
             }
-            if constexpr (MMA) {
-#pragma unroll
-              for (int k = 0; k < GramMma<N, FUSED>::NT; ++k) cg[k][0] = cg[k][1] = cg[k][2] = cg[k][3] = 0.f;
-            }
             if constexpr (PAIRS) {
 #pragma unroll
               for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
@@ -1440,17 +1358,8 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
           if constexpr (BLOCKED) {
             bwd_grads_slice<T, P, N, FUSED, PROJ, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
-            if constexpr (MMA) {
-              bwd_gram_mma_slice<T, N, FUSED>(cg, gs, xs, us, fs, reinterpret_cast<const uint8_t*>(&st.zrow),
-                                              geo.pitch, len, lane);
-              if (p == ns - 1) {
-                bwd_gram_mma_store<N, FUSED>(gram, cg, lane);
-                bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
-              }
-            } else {
-              bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
-              if (p == ns - 1) bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
-            }
+            bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
+            if (p == ns - 1) bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
           } else {
             if constexpr (PAIRS) {
               bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
@@ -1508,15 +1417,15 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   int64_t sl = D;
   int tpi = 1;
   if (tok_bytes > max_stage) {
-    if (tune.stage_bytes > 0) {
-      // tuned: the fewest slices of at most the target each, split evenly
-      // (multiples of 64 elements)
-      const int64_t target = std::min<int64_t>(tune.stage_bytes, max_stage);
-      const int64_t ns = (tok_bytes + target - 1) / target;
-      sl = ((D + ns - 1) / ns + 63) / 64 * 64;
-    } else {
-      sl = std::max<int64_t>(64, ((16 * 1024) / (rows * esize)) / 64 * 64);
-    }
+    // a token wider than a stage: the fewest slices of at most the target
+    // each (24 KB unless tuned), split evenly in multiples of 64 elements.
+    // Measured on B200 against slices of a fixed ~16 KB, whose last slice is
+    // a short remainder (n = 8, D = 1024: 448 + 448 + 128 elements, against
+    // 2 x 512): backward +29% there, +18-19% at D = 2048, 4096, +9% at n = 6,
+    // D = 4096; mix-write backward (n = 8, m = 4, D = 1024) +26%.
+    const int64_t target = tune.stage_bytes > 0 ? std::min<int64_t>(tune.stage_bytes, max_stage) : max_stage;
+    const int64_t ns = (tok_bytes + target - 1) / target;
+    sl = ((D + ns - 1) / ns + 63) / 64 * 64;
     if (sl >= D) sl = D;
   } else if (tok_bytes < item_target) {
     tpi = static_cast<int>(std::min<int64_t>(8, item_target / tok_bytes));
