@@ -42,6 +42,9 @@
 #include <type_traits>
 #include <utility>
 
+#include <cuda.h>  // CUtensorMap (the tensor maps are encoded through the runtime's driver entry point)
+#include <cudaTypedefs.h>
+
 #include "mix_kernels.cuh"
 
 namespace hc {
@@ -74,6 +77,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Tensor maps of the ring's inputs for tokens cut into slices (see
+// ring_issue): one per input tensor, a 3-D view [rows][D / 64][64] of it.
+struct alignas(64) RingMaps {
+  CUtensorMap m[4];
+};
+constexpr int kTmaChunk = 64;  // elements in the innermost box dimension
+
+// 3-D tensor copy global -> this CTA's shared memory through a tensor map in
+// kernel-parameter space (no multicast; one destination CTA).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 1-D bulk copy global -> this CTA's shared memory (one destination CTA).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -190,6 +211,7 @@ struct WarpGeometry {
   int producers;    // lanes of warp 0 that issue fills (1 <= producers <= stages)
   uint32_t wait_limit;  // polls of a data wait before it gives up
   unsigned int* status; // the library's status word (device-mapped host memory), or nullptr
+  int tma;              // slices are copied through the tensor maps (ns > 1 only)
 };
 
 
@@ -205,15 +227,31 @@ constexpr int warp_cap(bool bwd, int n) { return bwd ? bwd_warp_cap_max() : fwd_
 
 // Issue the bulk copies of one item (cnt consecutive tokens, or one slice of
 // one token) into a stage. Stage layout: [tensor][token][row][pitch].
+// A slice through the tensor maps (geo.tma) is ONE 3-D tensor copy per
+// tensor: box [rows][sl / 64][64] at (0, d0 / 64, t0 * rows), landing as
+// [row][sl], the x coordinate always 0; the part of a short last slice past
+// D is zero-filled and counted in the transaction bytes like the rest of the
+// box. Otherwise a slice is one 1-D copy per row.
 template <typename T, int NIN>
-__device__ __forceinline__ void ring_issue(const WarpGeometry& geo, int64_t D, uint8_t* stage, uint64_t* bar,
-                                           int64_t t0, int cnt, int p, const void* const* base, const int* rows) {
+__device__ __forceinline__ void ring_issue(const WarpGeometry& geo, const RingMaps* maps, int64_t D,
+                                           uint8_t* stage, uint64_t* bar, int64_t t0, int cnt, int p,
+                                           const void* const* base, const int* rows) {
   constexpr int es = sizeof(T);
   const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
   const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
   int rtot = 0;
 #pragma unroll
   for (int k = 0; k < NIN; ++k) rtot += rows[k];
+  if (geo.tma) {
+    mbar_expect_tx(bar, static_cast<uint32_t>(rtot * geo.sl * es));
+    uint8_t* dst = stage;
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) {
+      tma_load_3d(dst, &maps->m[k], 0, static_cast<int>(d0 / kTmaChunk), static_cast<int>(t0 * rows[k]), bar);
+      dst += static_cast<size_t>(rows[k]) * geo.pitch * es;
+    }
+    return;
+  }
   mbar_expect_tx(bar, static_cast<uint32_t>(cnt * rtot * len * es));
   uint8_t* dst = stage;
 #pragma unroll
@@ -303,7 +341,7 @@ struct ProducerCursor {
 template <typename T, int NIN>
 __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& geo, uint8_t* smem, int64_t D,
                                              int64_t t_begin, int ntok, int nunits, const void* const* base,
-                                             const int* rows, int lane) {
+                                             const int* rows, int lane, const RingMaps* maps = nullptr) {
   const int S = geo.stages, C = geo.consumers, P = geo.producers;
   if (P == 1) {
     int s = 0;
@@ -324,7 +362,7 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
           }
           const int u = g0 + w;
           const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-          ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
+          ring_issue<T, NIN>(geo, maps, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
                              t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
           __threadfence_block();  // the arrive.expect_tx above is visible before the tag
           st.tag[s] = k;
@@ -355,7 +393,7 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
       if (!fail) {
         const int u = c.g0 + c.w;
         const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-        ring_issue<T, NIN>(geo, D, smem + static_cast<size_t>(c.s) * geo.stage_bytes, &st.full[c.s],
+        ring_issue<T, NIN>(geo, maps, D, smem + static_cast<size_t>(c.s) * geo.stage_bytes, &st.full[c.s],
                            t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, c.p, base, rows);
         st.issued[c.s] = 1;
         st.last_parity[c.s] = c.ph;
@@ -744,7 +782,7 @@ __device__ __forceinline__ void fwd_slice(const MixFwdArgs& a, const TokParams<P
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
 __global__ void __launch_bounds__(fwd_warp_cap(N) * 32, 1)
-mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
+mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
   constexpr int NS = FUSED ? 1 : N;
   constexpr int es = sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
@@ -767,7 +805,7 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo) {
     if (lane < geo.producers) {
       const void* base[2] = {a.x, a.src};
       const int rows[2] = {N, NS};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
+      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -1267,7 +1305,7 @@ __device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, const TokPa
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK>
 __global__ void __launch_bounds__(bwd_warp_cap(N, BLK) * 32, 1)
-mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
+mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
   constexpr int es = sizeof(T);
@@ -1304,7 +1342,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo) {
         rows[2] = 1;
         rows[3] = 1;
       }
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -1447,6 +1485,7 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
   geo.wait_limit = wait_poll_limit();
   geo.status = nullptr;  // set by the launcher, which knows the stream
+  geo.tma = 0;           // set by the launcher once it has the tensor maps
   return true;
 }
 
@@ -1521,6 +1560,53 @@ inline int launch_ring(void (*kernel)(KArgs...), int grid, dim3 block, int smem_
   return HC_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); nullptr when the driver does not provide it.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor maps for a ring whose tokens are cut into slices: tensor k is viewed
+// as [T * rows[k]][D / 64][64] elements, box [rows[k]][sl / 64][64]. Sets
+// geo.tma when every map is encoded; otherwise the ring keeps one copy per
+// row. Needs D % 64 == 0, 16-byte aligned bases (the ring already does) and
+// row coordinates within int32.
+#ifndef HC_TMA
+#define HC_TMA 1  // build flag: 0 copies every slice row by row (measurements)
+#endif
+inline void ring_tensor_maps(WarpGeometry& geo, RingMaps& maps, const void* const* base, const int* rows, int nin,
+                             int64_t T, int64_t D, int esize) {
+  geo.tma = 0;
+  if (!HC_TMA || geo.ns <= 1 || D % kTmaChunk != 0 || geo.sl % kTmaChunk != 0 || nin > 4) return;
+  const auto encode = tensor_map_encoder();
+  if (!encode) return;
+  const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  for (int k = 0; k < nin; ++k) {
+    if (T * rows[k] >= (int64_t(1) << 31)) return;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kTmaChunk), static_cast<cuuint64_t>(D / kTmaChunk),
+                                static_cast<cuuint64_t>(T * rows[k])};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kTmaChunk) * esize, static_cast<cuuint64_t>(D) * esize};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTmaChunk), static_cast<cuuint32_t>(geo.sl / kTmaChunk),
+                               static_cast<cuuint32_t>(rows[k])};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode(&maps.m[k], dt, 3, const_cast<void*>(base[k]), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return;
+  }
+  geo.tma = 1;
+}
+
 template <typename KernelT>
 inline int warp_prepare(KernelT* kernel, int smem_bytes) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
@@ -1538,13 +1624,19 @@ template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, cudaStream_t s) {
   WarpGeometry geo = geo_in;
   geo.status = timeout_word(s);
+  RingMaps maps;
+  {
+    const void* base[2] = {a.x, a.src};
+    const int rows[2] = {n, FUSED ? 1 : n};
+    ring_tensor_maps(geo, maps, base, rows, 2, a.T, a.D, sizeof(T));
+  }
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
     auto* k = mix_fwd_warp_kernel<T, P, NN, FUSED, PROJ, fwd_lane_words(NN)>;       \
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;            \
-    if (int rc = launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo)) return rc; \
+    if (int rc = launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps)) return rc; \
     break;                                                              \
   }
     HC_CASE(1) HC_CASE(2) HC_CASE(3) HC_CASE(4) HC_CASE(5) HC_CASE(6) HC_CASE(7) HC_CASE(8)
@@ -1555,21 +1647,22 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, 
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK>
-int launch_bwd_kernel(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
+int launch_bwd_kernel(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
+                      cudaStream_t s) {
   auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK>;
   if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-  return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
+  return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps);
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ>
-int launch_bwd_one(const WarpGeometry& geo, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
+int launch_bwd_one(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
   if constexpr (bwd_blocked_n(N) && PROJ) {
-    return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+    return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
   } else {
     if constexpr (bwd_blocked_n(N)) {
-      if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, block, a, s);
+      if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
     }
-    return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, block, a, s);
+    return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, maps, block, a, s);
   }
 }
 
@@ -1577,11 +1670,17 @@ template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_bwd_warp(int n, const WarpGeometry& geo_in, const MixBwdArgs& a, cudaStream_t s) {
   WarpGeometry geo = geo_in;
   geo.status = timeout_word(s);
+  RingMaps maps;
+  {
+    const void* base[4] = {a.g, a.x, a.gu, a.f};
+    const int rows[4] = {n, n, 1, 1};
+    ring_tensor_maps(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T));
+  }
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
   case NN: {                                                            \
-    if (int rc = launch_bwd_one<T, P, NN, FUSED, PROJ>(geo, block, a, s)) return rc; \
+    if (int rc = launch_bwd_one<T, P, NN, FUSED, PROJ>(geo, maps, block, a, s)) return rc; \
     break;                                                              \
   }
     HC_CASE(1) HC_CASE(2) HC_CASE(3) HC_CASE(4) HC_CASE(5) HC_CASE(6) HC_CASE(7) HC_CASE(8)
