@@ -103,7 +103,7 @@ class ClockSampler:
     background thread; ``window(t0, t1)`` summarises the samples taken while
     the timed region ran."""
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.samples: list[tuple[float, int, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -210,6 +210,44 @@ def barrier(world: int):
         torch.distributed.barrier()
 
 
+class numa_local:
+    """Runs its body on the host CPUs nearest to a GPU (NVML's CPU affinity of
+    the device, read-only), then restores the thread's affinity. Pinned host
+    buffers allocated inside land on that GPU's NUMA node (first touch), so
+    their DMA does not cross the socket interconnect. No-op where NVML or
+    sched_setaffinity is unavailable."""
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.saved = None
+
+    def _gpu_cpus(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = int(visible.split(",")[self.device_index]) if visible else self.device_index
+        h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+        words = (os.cpu_count() + 63) // 64
+        mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        return {64 * w + b for w, m in enumerate(mask) for b in range(64) if (m >> b) & 1}
+
+    def __enter__(self):
+        try:
+            cpus = self._gpu_cpus() & os.sched_getaffinity(0)
+            if cpus:
+                self.saved = os.sched_getaffinity(0)
+                os.sched_setaffinity(0, cpus)
+        except Exception:
+            self.saved = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+        return False
+
+
 # ---------------------------------------------------------------- B200 arm
 class FusedRunner:
     """Direct C-ABI launches of the fused forward and backward on resident
@@ -282,7 +320,6 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
         e[1].record()
     torch.cuda.synchronize(device)
     barrier(world)
-    t1 = time.perf_counter()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
         flush.fill_(float(i))
@@ -293,11 +330,12 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
         runner.bwd()
         e[2].record()
     torch.cuda.synchronize(device)
+    t2 = time.perf_counter()
     step_ms = [e[0].elapsed_time(e[1]) for e in steps_ev]
     fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
     bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
     del flush
-    return {"step_ms": step_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t1), "launches": 2 * steps}
+    return {"step_ms": step_ms, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "wall": (t0, t2), "launches": 2 * steps}
 
 
 class ExpmRunner:
@@ -390,7 +428,8 @@ def time_e2e(device, steps, warmup):
     current stream between them, ordered by events."""
     from hyperconnections_b200.ops import stream_mix_fused
 
-    host = [t.pin_memory() for t in fused_workload(TOKENS, N_STREAMS, BLOCK, seed=1)]
+    with numa_local(device.index):
+        host = [t.pin_memory() for t in fused_workload(TOKENS, N_STREAMS, BLOCK, seed=1)]
     h2d = sum(t.numel() * t.element_size() for t in host)
     comp = torch.cuda.current_stream(device)
     up = torch.cuda.Stream(device)
@@ -410,7 +449,8 @@ def time_e2e(device, steps, warmup):
         torch.autograd.backward([u, x_out], [g_u, g_x])
         outs = [u.detach(), x_out.detach()] + [t.grad for t in leaves]
         if outs_host is None:
-            outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+            with numa_local(device.index):
+                outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
         down.wait_stream(comp)
         with torch.cuda.stream(down):
             for dst, src in zip(outs_host, outs):
