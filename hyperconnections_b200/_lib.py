@@ -15,7 +15,10 @@ from typing import Optional
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhcops.so")
+# The in-tree build, unless HC_LIBHCOPS names another build of the same ABI
+# (read once, when this module is imported: importing the package loads the
+# library, so a later change of LIB_PATH does not switch builds).
+LIB_PATH = os.environ.get("HC_LIBHCOPS") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhcops.so")
 
 HC_DTYPE_F32 = 0
 HC_DTYPE_F16 = 1
