@@ -212,6 +212,7 @@ struct WarpGeometry {
   uint32_t wait_limit;  // polls of a data wait before it gives up
   unsigned int* status; // the library's status word (device-mapped host memory), or nullptr
   int tma;              // slices are copied through the tensor maps (ns > 1 only)
+  int gram_mma;         // backward: the Gram on the tensor cores (rows padded by kGramMmaPad elements)
 };
 
 
@@ -281,6 +282,7 @@ struct RingState {
   uint32_t last_parity[kRingMaxStages];
   int issued[kRingMaxStages];
   volatile int abort;
+  alignas(16) uint32_t zrow[4];  // 16 zero bytes: the tensor-core Gram's rows past the matrix or the slice
 };
 
 __device__ __forceinline__ void ring_init(RingState& st, int stages) {
@@ -293,6 +295,7 @@ __device__ __forceinline__ void ring_init(RingState& st, int stages) {
       st.last_parity[s] = 0;
     }
     st.abort = 0;
+    for (int i = 0; i < 4; ++i) st.zrow[i] = 0u;
     fence_mbar_init();
   }
   __syncthreads();
@@ -1233,6 +1236,123 @@ __device__ __forceinline__ void bwd_gram_slice(float* gram, const uint8_t* gsb, 
   }
 }
 
+// ------------------------------------- pass B on the tensor cores (bf16 / fp16)
+// For half-precision streams the slice's Gram M = A B^T (A = [g; g_u] rows, B
+// = [x; f] rows, K = the slice's elements) is a warp-level contraction:
+// ldmatrix loads the rows straight from the ring stage and
+// mma.sync.m16n8k16 (fp32 accumulation; the product of two bf16 / fp16 values
+// is exact in fp32) accumulates a 16 x 8 tile per instruction, one or two
+// tiles for NA <= 8 or 9 columns. Rows and columns past NA, and the second
+// half of a 16-element step past the slice's end (slices are multiples of 8
+// elements), read the ring's zeroed 16-byte row. The accumulators stay in
+// registers over all slices of the token; at its last slice they are written
+// to the warp's Gram, whose finish is the CUDA-core path's.
+//
+// An 8 x 8 ldmatrix reads the same 16 bytes of 8 rows; with rows a multiple of
+// 128 bytes apart all eight sit in the same four banks (an 8-way conflict), so
+// the rings of this path pad every row by 16 bytes (pitch = slice + 8
+// elements): row r starts 4 r banks further and the 8 rows cover all 32.
+template <typename T> struct MmaKind;
+template <> struct MmaKind<__nv_bfloat16> {
+  __device__ static __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+template <> struct MmaKind<__half> {
+  __device__ static __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+#ifndef HC_GRAM_MMA
+#define HC_GRAM_MMA 1  // build flag: 0 keeps pass B on the FMA pipe for every dtype (measurements)
+#endif
+constexpr bool gram_mma_dtype(int esize) { return HC_GRAM_MMA && esize == 2; }
+constexpr int kGramMmaPad = 8;  // elements of padding per ring row on this path (16 bytes)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+template <int N, bool FUSED>
+struct GramMma {
+  static constexpr int NA = N + (FUSED ? 1 : 0);
+  static constexpr int NT = (NA + 7) / 8;  // n8 tiles of columns
+};
+
+// Accumulates one slice of the token's Gram into c (see above). gsb, xsb,
+// usb, fsb: the stage's g, x, g_u and f rows; zrow: 16 zero bytes in shared
+// memory.
+template <typename T, int N, bool FUSED>
+__device__ __forceinline__ void bwd_gram_mma_slice(float (&c)[GramMma<N, FUSED>::NT][4], const uint8_t* gsb,
+                                                   const uint8_t* xsb, const uint8_t* usb, const uint8_t* fsb,
+                                                   const uint8_t* zrow, int pitch, int len, int lane) {
+  constexpr int NT = GramMma<N, FUSED>::NT;
+  constexpr int es = sizeof(T);
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  const int q = lane >> 3;
+  // A: matrix q holds rows (q & 1) * 8 + (lane & 7), elements (q >> 1) * 8 + [0, 8)
+  const int ar = (q & 1) * 8 + (lane & 7);
+  const uint8_t* arow = ar < N ? gsb + ar * rowb : (FUSED && ar == N ? usb : nullptr);
+  const int akof = (q >> 1) * 8;
+  // B: matrix q holds rows (columns of M) (q >> 1) * 8 + (lane & 7), elements (q & 1) * 8 + [0, 8)
+  const int bj = (q >> 1) * 8 + (lane & 7);
+  const uint8_t* brow = bj < N ? xsb + bj * rowb : (FUSED && bj == N ? fsb : nullptr);
+  const int bkof = (q & 1) * 8;
+  const uint32_t z = smem_u32(zrow);
+  for (int k0 = 0; k0 < len; k0 += 16) {
+    const uint32_t aaddr = (arow && k0 + akof < len) ? smem_u32(arow + (k0 + akof) * es) : z;
+    const uint32_t baddr = (brow && k0 + bkof < len) ? smem_u32(brow + (k0 + bkof) * es) : z;
+    uint32_t af[4];
+    ldsm_x4(af, aaddr);
+    if constexpr (NT == 2) {
+      uint32_t bf[4];
+      ldsm_x4(bf, baddr);
+      MmaKind<T>::mma(c[0], af, bf[0], bf[1]);
+      MmaKind<T>::mma(c[NT - 1], af, bf[2], bf[3]);
+    } else {
+      uint32_t b0, b1;
+      ldsm_x2(b0, b1, baddr);  // lanes 0-15 give the addresses
+      MmaKind<T>::mma(c[0], af, b0, b1);
+    }
+  }
+}
+
+// The token's Gram from the accumulators into the warp's Gram (row-major
+// NA x NA); c[t][0..1] hold row lane / 4, c[t][2..3] row lane / 4 + 8, at
+// columns 8 t + 2 (lane % 4) + {0, 1}.
+template <int N, bool FUSED>
+__device__ __forceinline__ void bwd_gram_mma_store(float* gram, const float (&c)[GramMma<N, FUSED>::NT][4],
+                                                   int lane) {
+  constexpr int NA = GramMma<N, FUSED>::NA;
+  constexpr int NT = GramMma<N, FUSED>::NT;
+  const int r = lane >> 2;
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int col = 8 * t + 2 * (lane & 3);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r + 8 * h;
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        if (row < NA && col + e < NA) gram[row * NA + col + e] = c[t][2 * h + e];
+    }
+  }
+  __syncwarp();
+}
+
 // The token's parameter gradients from its Gram, then the Gram cleared for
 // the warp's next token. With the projection the extra sums are linear in
 // the plain Gram M = G X^T: rho_i = sum_d g_i v^T x = sum_j v_j M_ij and
@@ -1303,9 +1423,10 @@ __device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, const TokPa
   __syncwarp();
 }
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK>
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK, bool MMA>
 __global__ void __launch_bounds__(bwd_warp_cap(N, BLK) * 32, 1)
 mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
+  static_assert(!MMA || (BLK && sizeof(T) == 2), "the tensor-core Gram is a blocked, half-precision path");
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
   constexpr int es = sizeof(T);
@@ -1351,6 +1472,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     using Params = std::conditional_t<PAIRS, TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
     Params pr;
     float acc[BLOCKED ? 1 : L::kPad];
+    float cg[MMA ? GramMma<N, FUSED>::NT : 1][4];  // tensor-core Gram accumulators of the token
     float2 acc2[PAIRS ? L::kAcc : 1];
     float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
     if constexpr (BLOCKED) {
@@ -1385,6 +1507,10 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
 #pragma unroll
               for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
             }
+            if constexpr (MMA) {
+#pragma unroll
+              for (int k = 0; k < GramMma<N, FUSED>::NT; ++k) cg[k][0] = cg[k][1] = cg[k][2] = cg[k][3] = 0.f;
+            }
             if constexpr (PAIRS) {
 #pragma unroll
               for (int k = 0; k < L::kAcc; ++k) acc2[k] = make_float2(0.f, 0.f);
@@ -1396,8 +1522,17 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
           if constexpr (BLOCKED) {
             bwd_grads_slice<T, P, N, FUSED, PROJ, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
-            bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
-            if (p == ns - 1) bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
+            if constexpr (MMA) {
+              bwd_gram_mma_slice<T, N, FUSED>(cg, gs, xs, us, fs, reinterpret_cast<const uint8_t*>(st.zrow),
+                                              geo.pitch, len, lane);
+              if (p == ns - 1) {
+                bwd_gram_mma_store<N, FUSED>(gram, cg, lane);
+                bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
+              }
+            } else {
+              bwd_gram_slice<T, N, FUSED, W, 0>(gram, gs, xs, us, fs, geo.pitch, len, lane);
+              if (p == ns - 1) bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
+            }
           } else {
             if constexpr (PAIRS) {
               bwd_slice2<T, P, N, FUSED, PROJ, W>(a, pr, acc2, gs, xs, us, fs, geo.pitch, t, d0, len, lane);
@@ -1441,7 +1576,7 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 //   * tokens smaller than the item target are grouped, tpi per item, so that
 //     one bulk copy per tensor moves several tokens.
 inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
-                          int num_sms, bool bwd) {
+                          int num_sms, bool bwd, int pad = 0) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
   const MixTuning tune = mix_tuning();
   const int budget = 200 * 1024;
@@ -1471,8 +1606,8 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   geo.tpi = tpi;
   geo.sl = static_cast<int>(sl);
   geo.ns = static_cast<int>((D + sl - 1) / sl);
-  geo.pitch = geo.sl;
-  geo.stage_bytes = static_cast<int>(tpi * rows * sl * esize);
+  geo.pitch = geo.sl + (geo.ns > 1 ? pad : 0);  // padded rows: only slices, copied row by row
+  geo.stage_bytes = static_cast<int>(tpi * rows * geo.pitch * esize);
   int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
   if (tune.stages > 0) stages = std::min(stages, tune.stages);
   int consumers = std::min(warp_cap_ - 1, stages - 2);
@@ -1486,6 +1621,7 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   geo.wait_limit = wait_poll_limit();
   geo.status = nullptr;  // set by the launcher, which knows the stream
   geo.tma = 0;           // set by the launcher once it has the tensor maps
+  geo.gram_mma = 0;
   return true;
 }
 
@@ -1524,6 +1660,12 @@ inline void prefer_producers(WarpGeometry& geo) {
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, int n, int64_t T, int64_t D,
                           int esize, int num_sms) {
   if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
+  if (bwd && geo.ns > 1 && bwd_blocked(n, proj, geo.ns) && gram_mma_dtype(esize)) {
+    // the tensor-core Gram reads 8 rows per ldmatrix: pad the rows off the bank period
+    if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd, kGramMmaPad))
+      return false;
+    geo.gram_mma = 1;
+  }
   if (bwd) {
     const int cap = bwd_warp_cap(n, bwd_blocked(n, proj, geo.ns));
     geo.consumers = std::min(geo.consumers, cap - 1);
@@ -1587,7 +1729,8 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 inline void ring_tensor_maps(WarpGeometry& geo, RingMaps& maps, const void* const* base, const int* rows, int nin,
                              int64_t T, int64_t D, int esize) {
   geo.tma = 0;
-  if (!HC_TMA || geo.ns <= 1 || D % kTmaChunk != 0 || geo.sl % kTmaChunk != 0 || nin > 4) return;
+  if (!HC_TMA || geo.ns <= 1 || geo.pitch != geo.sl || D % kTmaChunk != 0 || geo.sl % kTmaChunk != 0 || nin > 4)
+    return;
   const auto encode = tensor_map_encoder();
   if (!encode) return;
   const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
@@ -1646,21 +1789,33 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, 
   return launch_status();
 }
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK>
+template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK, bool MMA = false>
 int launch_bwd_kernel(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
                       cudaStream_t s) {
-  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK>;
+  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK, MMA>;
   if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
   return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps);
+}
+
+// The blocked kernel, with its Gram on the tensor cores when the geometry
+// padded the ring's rows for it (half-precision streams cut into slices).
+template <typename T, typename P, int N, bool FUSED, bool PROJ>
+int launch_bwd_blocked(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
+                       cudaStream_t s) {
+  if constexpr (gram_mma_dtype(sizeof(T))) {
+    if (geo.gram_mma) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true, true>(geo, maps, block, a, s);
+  }
+  if (geo.gram_mma) return HC_ERR_LAUNCH;  // not reached: the geometry pads only half-precision rings
+  return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
 }
 
 template <typename T, typename P, int N, bool FUSED, bool PROJ>
 int launch_bwd_one(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a, cudaStream_t s) {
   if constexpr (bwd_blocked_n(N) && PROJ) {
-    return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
+    return launch_bwd_blocked<T, P, N, FUSED, PROJ>(geo, maps, block, a, s);
   } else {
     if constexpr (bwd_blocked_n(N)) {
-      if (geo.ns > 1) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
+      if (geo.ns > 1) return launch_bwd_blocked<T, P, N, FUSED, PROJ>(geo, maps, block, a, s);
     }
     return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, maps, block, a, s);
   }

@@ -104,6 +104,19 @@ def test_fused_half(dtype, n, D):
     check(u, x_out, grads, inputs, None, rel=False)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [5, 6, 7, 8])
+@pytest.mark.parametrize("D", [1536, 1800])
+def test_fused_half_sliced_gram(dtype, n, D):
+    """Tokens cut into slices at n >= 5 with half-precision streams: the
+    blocked backward with its Gram on the tensor cores (ring rows padded,
+    copied row by row). At D = 1800 the last slice is not a multiple of 16
+    elements (its last k-step reads the zero row)."""
+    inputs = workload(23, n, D, dtype, seed=11 * n + D)
+    u, x_out, grads = run(*inputs)
+    check(u, x_out, grads, inputs, None, rel=False)
+
+
 FUSED = load_golden("fused.npz")
 
 
