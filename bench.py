@@ -17,7 +17,9 @@ The batched matrix exponential (65,536 skew 4x4, forward + Frechet backward)
 is reported alongside in matrices/s.
 
 Timing: CUDA events on the launching stream around each kernel, L2 flushed
-(a 256 MiB write) between steps outside the events, barrier + synchronize
+between steps outside the events (a 256 MiB write, then a 256 MiB read that
+writes the flush's dirty lines back; ``write_flush`` repeats the step after
+the write alone), barrier + synchronize
 around the K timed steps, max over ranks. Under torchrun every rank runs one
 full batch of the workload on its own GPU (its shard of an N x 16,384-token
 global batch, seeded by rank) with no collective on the data path (weak
@@ -293,7 +295,28 @@ class FusedRunner:
         self._check(rc, "hc_fused_bwd")
 
 
-def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0, shard=None):
+class L2Flush:
+    """Evicts L2 (126 MB) between timed steps, outside the events. "clean"
+    (the default): a 256 MiB write, so that no input of the step stays in L2,
+    then a 256 MiB read of another buffer, which writes the first buffer's
+    dirty lines back before the step starts; the step begins cold on a clean
+    L2, the state ncu's cache control gives a profiled kernel. "write": the
+    write alone; the timed step then also pays the write-back of up to ~126 MB
+    of the flush's own dirty lines."""
+
+    def __init__(self, device, mode: str = "clean"):
+        words = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(words, dtype=torch.float32, device=device)
+        self.r = torch.ones(words, dtype=torch.float32, device=device) if mode == "clean" else None
+        self.sink = torch.empty((), dtype=torch.float32, device=device)
+
+    def __call__(self, i: int):
+        self.w.fill_(float(i))
+        if self.r is not None:
+            torch.sum(self.r, dim=0, out=self.sink)
+
+
+def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, seed=0, shard=None, flush_mode="clean"):
     """Two timed passes of `steps` fused steps each, L2 flushed before every
     step outside the events. Pass 1 records events only around the step
     (forward then backward back to back, as a training step runs them: the
@@ -301,9 +324,9 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
     dependent launch); its times are the headline. Pass 2 adds an event between
     the kernels for the per-kernel split and the dominant kernel's roofline."""
     runner = FusedRunner(device, T=T, n=n, D=D, seed=seed, shard=shard)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    for _ in range(warmup):
-        flush.fill_(1.0)
+    flush = L2Flush(device, flush_mode)
+    for i in range(warmup):
+        flush(i)
         runner.fwd()
         runner.bwd()
     torch.cuda.synchronize(device)
@@ -312,7 +335,7 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
     t0 = time.perf_counter()
     steps_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
     for i in range(steps):
-        flush.fill_(float(i))  # evict L2 between steps, outside the events
+        flush(i)  # evict L2 between steps, outside the events
         e = steps_ev[i]
         e[0].record()
         runner.fwd()
@@ -322,7 +345,7 @@ def time_fused(device, steps, warmup, world, T=TOKENS, n=N_STREAMS, D=BLOCK, see
     barrier(world)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
-        flush.fill_(float(i))
+        flush(i)
         e = evs[i]
         e[0].record()
         runner.fwd()
@@ -372,14 +395,14 @@ def time_expm(device, steps, warmup, B=EXPM_BATCH, n=EXPM_N, split=False):
     (C-ABI launches), L2 flushed between steps; ms per step (and, with
     split=True, also the forward's ms per step)."""
     runner = ExpmRunner(device, B, n)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    flush = L2Flush(device)
     for _ in range(warmup):
         runner.fwd()
         runner.bwd()
     torch.cuda.synchronize(device)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
-        flush.fill_(float(i))
+        flush(i)
         evs[i][0].record()
         runner.fwd()
         evs[i][1].record()
@@ -562,7 +585,9 @@ CONFIG = {
     "workload": "fused hyper-connection step fwd+bwd: x[16,1024,4,768] bf16, f[16,1024,768] bf16, "
                 "H[16,1024,4,4]=expm(skew) fp32, alpha/beta[16,1024,4]=softmax fp32, seed 0",
     "tokens": TOKENS, "n_streams": N_STREAMS, "block_size": BLOCK,
-    "l2": "flushed between steps (256 MiB write, outside the timed events)",
+    "l2": ("flushed between steps outside the timed events: a 256 MiB write, then a 256 MiB read that writes "
+           "the flush's own dirty lines back (inputs cold, L2 clean); write_flush repeats the step with the "
+           "write alone"),
 }
 
 
@@ -697,6 +722,12 @@ def run_b200(args):
     else:
         strong_ms = step_ms_max
     strong_value = (fb + bb) / (strong_ms * 1e-3) / 1e9
+    # the same step after a write-only L2 flush (see L2Flush)
+    wf = time_fused(device, args.steps, args.warmup, world, seed=dist_env()[1], flush_mode="write")
+    wf_ms = max_over_ranks(float(np.mean(wf["step_ms"])), world, device)
+    write_flush = {"value": world * (fb + bb) / (wf_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": wf_ms,
+                   "kernels_ms": {"hc_fused_fwd": float(np.mean(wf["fwd_ms"])),
+                                  "hc_fused_bwd": float(np.mean(wf["bwd_ms"]))}}
 
     expm_ms, expm_fwd_ms = time_expm(device, max(5, min(args.steps, 50)), max(3, args.warmup), split=True)
     expm_step = float(np.mean(expm_ms))
@@ -743,6 +774,7 @@ def run_b200(args):
             "kernels_ms": {"hc_fused_fwd": fwd_ms, "hc_fused_bwd": bwd_ms,
                            "note": "separate pass with an event between the kernels"},
             "rank_ms_per_step": rank_ms,
+            "write_flush": write_flush,
             "strong_scaling": {"value": strong_value, "unit": "GB/s", "ms_per_step": strong_ms,
                                "tokens_per_rank": TOKENS // world,
                                "what": "the same step with the 16,384-token batch split over the ranks "
@@ -854,14 +886,14 @@ class RwRunner:
 
 def time_launches(device, fns, steps, warmup):
     """Mean device ms of each callable in `fns`, L2 flushed between steps."""
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    flush = L2Flush(device)
     for _ in range(warmup):
         for fn in fns:
             fn()
     torch.cuda.synchronize(device)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)] for _ in range(steps)]
     for i in range(steps):
-        flush.fill_(float(i))
+        flush(i)
         evs[i][0].record()
         for k, fn in enumerate(fns):
             fn()

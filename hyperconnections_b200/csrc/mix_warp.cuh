@@ -83,6 +83,22 @@ struct alignas(64) RingMaps {
   CUtensorMap m[4];
 };
 constexpr int kTmaChunk = 64;  // elements in the innermost box dimension
+// Swizzled stages of the tensor-core Gram path (see gram_mma_slice): each
+// tensor's region is 1024-byte aligned (the 128-byte swizzle repeats every 8
+// lines), and the ring's base is aligned up to 1024 bytes inside kSwzAlign
+// bytes of slack.
+constexpr int kSwzAlign = 1024;
+__host__ __device__ constexpr int swz_region_bytes(int rows, int sl, int esize) {
+  return (rows * sl * esize + kSwzAlign - 1) / kSwzAlign * kSwzAlign;
+}
+// Address of byte eb of a slice row (eb % 16 + access size <= 16) of row r in
+// a swizzled region whose rows hold nc 128-byte lines each: line r * nc +
+// eb / 128, its 16-byte unit (eb / 16) % 8 stored at unit
+// ((eb / 16) % 8) ^ (line % 8).
+__device__ __forceinline__ const uint8_t* swz_at(const uint8_t* region, int nc, int r, int eb) {
+  const int line = r * nc + (eb >> 7);
+  return region + line * 128 + ((((eb >> 4) & 7) ^ (line & 7)) << 4) + (eb & 15);
+}
 
 // 3-D tensor copy global -> this CTA's shared memory through a tensor map in
 // kernel-parameter space (no multicast; one destination CTA).
@@ -212,7 +228,7 @@ struct WarpGeometry {
   uint32_t wait_limit;  // polls of a data wait before it gives up
   unsigned int* status; // the library's status word (device-mapped host memory), or nullptr
   int tma;              // slices are copied through the tensor maps (ns > 1 only)
-  int gram_mma;         // backward: the Gram on the tensor cores (rows padded by kGramMmaPad elements)
+  int gram_mma;         // backward Gram on the tensor cores: 0 no, kGramPadded or kGramSwizzled stages
 };
 
 
@@ -249,7 +265,8 @@ __device__ __forceinline__ void ring_issue(const WarpGeometry& geo, const RingMa
 #pragma unroll
     for (int k = 0; k < NIN; ++k) {
       tma_load_3d(dst, &maps->m[k], 0, static_cast<int>(d0 / kTmaChunk), static_cast<int>(t0 * rows[k]), bar);
-      dst += static_cast<size_t>(rows[k]) * geo.pitch * es;
+      // swizzled stages: 1024-byte aligned regions
+      dst += geo.gram_mma ? swz_region_bytes(rows[k], geo.sl, es) : static_cast<int>(rows[k]) * geo.pitch * es;
     }
     return;
   }
@@ -1063,10 +1080,14 @@ struct GramShape {
 #define HC_PASSA_PAIRS 1  // build flag: 0 runs pass A's grad_x as scalar FMA chains (measurements)
 #endif
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, int W>
+// SWZ: the stage's g and g_u regions are chunk-major swizzled (the tensor-core
+// Gram path, W == 1: a segment is one 64-element chunk); otherwise row-major
+// with `pitch` elements per row.
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool SWZ = false>
 __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
                                                 const uint8_t* gsb, const uint8_t* usb, int pitch, int64_t t,
-                                                int64_t d0, int len, int lane) {
+                                                int64_t d0, int len, int lane, int nc = 0) {
+  static_assert(!SWZ || (W == 1 && sizeof(T) == 2), "swizzled stages: 4-byte lane reads of 2-byte elements");
   using Wd = Word<T>;
   constexpr int K = Wd::K;
   constexpr int es = sizeof(T);
@@ -1079,9 +1100,15 @@ __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokPa
   for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
     const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> gw_[N], uw;
+    if constexpr (SWZ) {
 #pragma unroll
-    for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(gsb + eo + r * rowb);
-    if constexpr (FUSED) uw = lds_words<W>(usb + eo);
+      for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(swz_at(gsb, nc, r, static_cast<int>(eo)));
+      if constexpr (FUSED) uw = lds_words<W>(swz_at(usb, nc, 0, static_cast<int>(eo)));
+    } else {
+#pragma unroll
+      for (int r = 0; r < N; ++r) gw_[r] = lds_words<W>(gsb + eo + r * rowb);
+      if constexpr (FUSED) uw = lds_words<W>(usb + eo);
+    }
     uint32_t gxo[N][W], gfo[W];
 #pragma unroll
     for (int w = 0; w < W; ++w) {
@@ -1248,10 +1275,26 @@ __device__ __forceinline__ void bwd_gram_slice(float* gram, const uint8_t* gsb, 
 // registers over all slices of the token; at its last slice they are written
 // to the warp's Gram, whose finish is the CUDA-core path's.
 //
-// An 8 x 8 ldmatrix reads the same 16 bytes of 8 rows; with rows a multiple of
-// 128 bytes apart all eight sit in the same four banks (an 8-way conflict), so
-// the rings of this path pad every row by 16 bytes (pitch = slice + 8
-// elements): row r starts 4 r banks further and the 8 rows cover all 32.
+// Stage layouts of this path. An 8 x 8 ldmatrix reads the same 16 bytes of 8
+// rows; in the plain row-major stage the rows are a multiple of 128 bytes
+// apart and all eight sit in the same four banks (an 8-way conflict). Two
+// layouts avoid it:
+//   kGramSwizzled  one TMA tensor copy per tensor and slice with the 128-byte
+//                  swizzle, box [rows][sl / 64][64] as in the plain ring: a
+//                  tensor's region (1024-byte aligned) holds row r's chunk c
+//                  in 128-byte line L = r * nc + c (nc = sl / 64), its 16-byte
+//                  unit u at unit u ^ (L mod 8). Slices hold an odd number of
+//                  chunks, so the 8 rows of one chunk fall in 8 different
+//                  unit positions; a warp reading one line 4 bytes a lane
+//                  (pass A) still touches all 32 banks once. The part of the
+//                  last slice past D is zero-filled by the copy.
+//   kGramPadded    one bulk copy per row into rows padded by 16 bytes (pitch
+//                  sl + 8 elements): row r starts 4 r banks further.
+// Measured on B200 (fused backward, 16,384 tokens, bf16): the swizzled ring
+// is faster at even n (n = 8, D = 1024: 190 against 225 us; n = 6, D = 1024:
+// 147 against 179 us; within 1.5% at D = 2048, 4096), the padded one at odd
+// n (n = 7, D = 1536: 249 against 307 us; n = 5, D = 2048: 236 against
+// 311 us, where odd chunk counts make 28 KB stages and fewer consumers).
 template <typename T> struct MmaKind;
 template <> struct MmaKind<__nv_bfloat16> {
   __device__ static __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -1275,7 +1318,10 @@ template <> struct MmaKind<__half> {
 #define HC_GRAM_MMA 1  // build flag: 0 keeps pass B on the FMA pipe for every dtype (measurements)
 #endif
 constexpr bool gram_mma_dtype(int esize) { return HC_GRAM_MMA && esize == 2; }
-constexpr int kGramMmaPad = 8;  // elements of padding per ring row on this path (16 bytes)
+constexpr int kGramPadded = 1;    // geo.gram_mma: row copies into 16-byte padded rows
+constexpr int kGramSwizzled = 2;  // geo.gram_mma: swizzled TMA tensor copies
+constexpr int kGramPad = 8;       // elements of padding per row of kGramPadded stages
+
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -1292,29 +1338,47 @@ struct GramMma {
   static constexpr int NT = (NA + 7) / 8;  // n8 tiles of columns
 };
 
-// Accumulates one slice of the token's Gram into c (see above). gsb, xsb,
-// usb, fsb: the stage's g, x, g_u and f rows; zrow: 16 zero bytes in shared
-// memory.
-template <typename T, int N, bool FUSED>
-__device__ __forceinline__ void bwd_gram_mma_slice(float (&c)[GramMma<N, FUSED>::NT][4], const uint8_t* gsb,
-                                                   const uint8_t* xsb, const uint8_t* usb, const uint8_t* fsb,
-                                                   const uint8_t* zrow, int pitch, int len, int lane) {
-  constexpr int NT = GramMma<N, FUSED>::NT;
+// Address of byte eb of row r of a stage region: swizzled (nc lines a row)
+// or row-major with rowb bytes a row.
+template <bool SWZ>
+__device__ __forceinline__ const uint8_t* stage_at(const uint8_t* region, uint32_t rowb, int nc, int r, int eb) {
+  if constexpr (SWZ) {
+    return swz_at(region, nc, r, eb);
+  } else {
+    return region + r * rowb + eb;
+  }
+}
+
+// Accumulates one slice of a Gram M = A B^T into c (see above): A's rows are
+// A0 rows of region a0 then A1 rows of region a1 (at most 16), B's rows B0
+// rows of region b0 then B1 rows of region b1 (at most 16, (B0 + B1 + 7) / 8
+// tiles of 8 columns); rows past them read zrow (16 zero bytes in shared
+// memory). Padded stages: rowb bytes a row, and the second half of a
+// 16-element step past the slice's end (slices are multiples of 8 elements)
+// reads zrow; swizzled stages: nc lines a row, the box zero-filled past D.
+template <typename T, int A0, int A1, int B0, int B1, bool SWZ>
+__device__ __forceinline__ void gram_mma_slice(float (&c)[(B0 + B1 + 7) / 8][4], const uint8_t* a0,
+                                               const uint8_t* a1, const uint8_t* b0, const uint8_t* b1,
+                                               const uint8_t* zrow, uint32_t rowb, int nc, int len, int lane) {
+  constexpr int NT = (B0 + B1 + 7) / 8;
+  static_assert(A0 + A1 <= 16 && NT <= 2, "one 16-row A tile, at most two 8-column B tiles");
   constexpr int es = sizeof(T);
-  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
   const int q = lane >> 3;
   // A: matrix q holds rows (q & 1) * 8 + (lane & 7), elements (q >> 1) * 8 + [0, 8)
   const int ar = (q & 1) * 8 + (lane & 7);
-  const uint8_t* arow = ar < N ? gsb + ar * rowb : (FUSED && ar == N ? usb : nullptr);
+  const uint8_t* areg = ar < A0 ? a0 : (ar < A0 + A1 ? a1 : nullptr);
+  const int arow = ar < A0 ? ar : ar - A0;
   const int akof = (q >> 1) * 8;
   // B: matrix q holds rows (columns of M) (q >> 1) * 8 + (lane & 7), elements (q & 1) * 8 + [0, 8)
   const int bj = (q >> 1) * 8 + (lane & 7);
-  const uint8_t* brow = bj < N ? xsb + bj * rowb : (FUSED && bj == N ? fsb : nullptr);
+  const uint8_t* breg = bj < B0 ? b0 : (bj < B0 + B1 ? b1 : nullptr);
+  const int brow = bj < B0 ? bj : bj - B0;
   const int bkof = (q & 1) * 8;
   const uint32_t z = smem_u32(zrow);
   for (int k0 = 0; k0 < len; k0 += 16) {
-    const uint32_t aaddr = (arow && k0 + akof < len) ? smem_u32(arow + (k0 + akof) * es) : z;
-    const uint32_t baddr = (brow && k0 + bkof < len) ? smem_u32(brow + (k0 + bkof) * es) : z;
+    const bool ain = areg && (SWZ || k0 + akof < len), bin = breg && (SWZ || k0 + bkof < len);
+    const uint32_t aaddr = ain ? smem_u32(stage_at<SWZ>(areg, rowb, nc, arow, (k0 + akof) * es)) : z;
+    const uint32_t baddr = bin ? smem_u32(stage_at<SWZ>(breg, rowb, nc, brow, (k0 + bkof) * es)) : z;
     uint32_t af[4];
     ldsm_x4(af, aaddr);
     if constexpr (NT == 2) {
@@ -1323,21 +1387,19 @@ __device__ __forceinline__ void bwd_gram_mma_slice(float (&c)[GramMma<N, FUSED>:
       MmaKind<T>::mma(c[0], af, bf[0], bf[1]);
       MmaKind<T>::mma(c[NT - 1], af, bf[2], bf[3]);
     } else {
-      uint32_t b0, b1;
-      ldsm_x2(b0, b1, baddr);  // lanes 0-15 give the addresses
-      MmaKind<T>::mma(c[0], af, b0, b1);
+      uint32_t b0f, b1f;
+      ldsm_x2(b0f, b1f, baddr);  // lanes 0-15 give the addresses
+      MmaKind<T>::mma(c[0], af, b0f, b1f);
     }
   }
 }
 
-// The token's Gram from the accumulators into the warp's Gram (row-major
-// NA x NA); c[t][0..1] hold row lane / 4, c[t][2..3] row lane / 4 + 8, at
-// columns 8 t + 2 (lane % 4) + {0, 1}.
-template <int N, bool FUSED>
-__device__ __forceinline__ void bwd_gram_mma_store(float* gram, const float (&c)[GramMma<N, FUSED>::NT][4],
-                                                   int lane) {
-  constexpr int NA = GramMma<N, FUSED>::NA;
-  constexpr int NT = GramMma<N, FUSED>::NT;
+// The accumulators of an R x C Gram (R <= 16, C <= 16) into a row-major
+// R x C array in shared memory; c[t][0..1] hold row lane / 4, c[t][2..3] row
+// lane / 4 + 8, at columns 8 t + 2 (lane % 4) + {0, 1}.
+template <int R, int C>
+__device__ __forceinline__ void gram_mma_store(float* gram, const float (&c)[(C + 7) / 8][4], int lane) {
+  constexpr int NT = (C + 7) / 8;
   const int r = lane >> 2;
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
@@ -1347,7 +1409,7 @@ __device__ __forceinline__ void bwd_gram_mma_store(float* gram, const float (&c)
       const int row = r + 8 * h;
 #pragma unroll
       for (int e = 0; e < 2; ++e)
-        if (row < NA && col + e < NA) gram[row * NA + col + e] = c[t][2 * h + e];
+        if (row < R && col + e < C) gram[row * C + col + e] = c[t][2 * h + e];
     }
   }
   __syncwarp();
@@ -1423,14 +1485,19 @@ __device__ __forceinline__ void bwd_gram_finish(const MixBwdArgs& a, const TokPa
   __syncwarp();
 }
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK, bool MMA>
+template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool BLK, bool MMA, bool SWZ>
 __global__ void __launch_bounds__(bwd_warp_cap(N, BLK) * 32, 1)
 mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
   static_assert(!MMA || (BLK && sizeof(T) == 2), "the tensor-core Gram is a blocked, half-precision path");
+  static_assert(!SWZ || MMA, "swizzled stages belong to the tensor-core Gram");
   using L = BwdLayout<N, FUSED, PROJ>;
   constexpr int NIN = FUSED ? 4 : 2;
   constexpr int es = sizeof(T);
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // the swizzled stages of the tensor-core path start on a 1024-byte boundary
+  // (geo.smem_bytes holds kSwzAlign bytes of slack for it)
+  uint8_t* const smem = SWZ ? smem_raw + ((kSwzAlign - (smem_u32(smem_raw) & (kSwzAlign - 1))) & (kSwzAlign - 1))
+                            : smem_raw;
   __shared__ RingState st;
   // per-consumer Gram of the blocked path
   __shared__ float gram_all[BLK ? (kWarpMaxWarps - 1) * GramShape<N, FUSED>::SIZE : 1];
@@ -1520,13 +1587,22 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
           const uint8_t* xs = sb + nreg + tt * N * rowb;
           const uint8_t* us = sb + 2 * nreg + tt * rowb;
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
+          if constexpr (SWZ) {  // swizzled regions g, x, g_u, f (tpi == 1)
+            const int rn = swz_region_bytes(N, geo.sl, es), r1 = swz_region_bytes(1, geo.sl, es);
+            gs = sb;
+            xs = sb + rn;
+            us = sb + 2 * rn;
+            fs = sb + 2 * rn + r1;
+          }
           if constexpr (BLOCKED) {
-            bwd_grads_slice<T, P, N, FUSED, PROJ, W>(a, pr, gs, us, geo.pitch, t, d0, len, lane);
+            const int nc = geo.sl / kTmaChunk;
+            bwd_grads_slice<T, P, N, FUSED, PROJ, W, SWZ>(a, pr, gs, us, geo.pitch, t, d0, len, lane, nc);
             if constexpr (MMA) {
-              bwd_gram_mma_slice<T, N, FUSED>(cg, gs, xs, us, fs, reinterpret_cast<const uint8_t*>(st.zrow),
-                                              geo.pitch, len, lane);
+              constexpr int X = FUSED ? 1 : 0;  // the g_u row of A and the f row of B
+              gram_mma_slice<T, N, X, N, X, SWZ>(cg, gs, us, xs, fs, reinterpret_cast<const uint8_t*>(st.zrow), rowb,
+                                                 nc, len, lane);
               if (p == ns - 1) {
-                bwd_gram_mma_store<N, FUSED>(gram, cg, lane);
+                gram_mma_store<N + X, N + X>(gram, cg, lane);
                 bwd_gram_finish<P, N, FUSED, PROJ>(a, pr, gram, t, lane);
               }
             } else {
@@ -1575,11 +1651,28 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 //     per row slice);
 //   * tokens smaller than the item target are grouped, tpi per item, so that
 //     one bulk copy per tensor moves several tokens.
-inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
-                          int num_sms, bool bwd, int pad = 0) {
-  if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
+// Stages, consumers and shared memory of the ring for geo.stage_bytes; false
+// when fewer than 3 stages (or no consumer) fit.
+inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms, int slack_bytes = 0) {
   const MixTuning tune = mix_tuning();
   const int budget = 200 * 1024;
+  int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
+  if (tune.stages > 0) stages = std::min(stages, tune.stages);
+  int consumers = std::min(warp_cap_ - 1, stages - 2);
+  if (tune.warps > 0) consumers = std::min(consumers, tune.warps);
+  if (consumers < 1 || stages < 3) return false;
+  geo.stages = stages;
+  geo.consumers = consumers;
+  geo.producers = 1;
+  geo.smem_bytes = stages * geo.stage_bytes + slack_bytes;
+  geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
+  return true;
+}
+
+inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
+                          int num_sms, bool bwd) {
+  if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
+  const MixTuning tune = mix_tuning();
   const int64_t max_stage = 24 * 1024;
   // items of several small tokens: one bulk copy has a fixed cost, so small
   // items cap the copy rate (15 KB forward, 16 KB backward measured best; the
@@ -1606,18 +1699,9 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   geo.tpi = tpi;
   geo.sl = static_cast<int>(sl);
   geo.ns = static_cast<int>((D + sl - 1) / sl);
-  geo.pitch = geo.sl + (geo.ns > 1 ? pad : 0);  // padded rows: only slices, copied row by row
+  geo.pitch = geo.sl;
   geo.stage_bytes = static_cast<int>(tpi * rows * geo.pitch * esize);
-  int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
-  if (tune.stages > 0) stages = std::min(stages, tune.stages);
-  int consumers = std::min(warp_cap_ - 1, stages - 2);
-  if (tune.warps > 0) consumers = std::min(consumers, tune.warps);
-  if (consumers < 1 || stages < 3) return false;
-  geo.stages = stages;
-  geo.consumers = consumers;
-  geo.producers = 1;
-  geo.smem_bytes = stages * geo.stage_bytes;
-  geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
+  if (!ring_stage(geo, warp_cap_, T, num_sms)) return false;
   geo.wait_limit = wait_poll_limit();
   geo.status = nullptr;  // set by the launcher, which knows the stream
   geo.tma = 0;           // set by the launcher once it has the tensor maps
@@ -1657,14 +1741,37 @@ inline void prefer_producers(WarpGeometry& geo) {
   }
 }
 
+// max_gram: the tensor-core Gram stages allowed (kGramSwizzled: either;
+// kGramPadded: padded rows only, the launcher's fallback when the swizzled
+// tensor maps cannot be encoded).
 inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, int n, int64_t T, int64_t D,
-                          int esize, int num_sms) {
-  if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
+                          int esize, int num_sms, int max_gram = kGramSwizzled) {
+  const int rows = warp_rows(bwd, fused, n);
+  if (!ring_geometry(geo, rows, warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
   if (bwd && geo.ns > 1 && bwd_blocked(n, proj, geo.ns) && gram_mma_dtype(esize)) {
-    // the tensor-core Gram reads 8 rows per ldmatrix: pad the rows off the bank period
-    if (!ring_geometry(geo, warp_rows(bwd, fused, n), warp_cap(bwd, n), T, D, esize, num_sms, bwd, kGramMmaPad))
-      return false;
-    geo.gram_mma = 1;
+    // the tensor-core Gram (gram_mma_slice), on swizzled stages for even
+    // n and on padded rows for odd n (measured)
+    const WarpGeometry plain = geo;
+    bool ok = false;
+    if (max_gram >= kGramSwizzled && n % 2 == 0 && D % kTmaChunk == 0 && T * n < (int64_t(1) << 31)) {
+      if ((geo.sl / kTmaChunk) % 2 == 0) {  // an odd number of 128-byte lines a row
+        geo.sl += kTmaChunk;
+        geo.pitch = geo.sl;
+        geo.ns = static_cast<int>((D + geo.sl - 1) / geo.sl);
+      }
+      geo.stage_bytes =
+          2 * swz_region_bytes(n, geo.sl, esize) + (fused ? 2 * swz_region_bytes(1, geo.sl, esize) : 0);
+      geo.gram_mma = kGramSwizzled;
+      ok = geo.ns > 1 && ring_stage(geo, warp_cap(bwd, n), T, num_sms, kSwzAlign);
+    }
+    if (!ok && max_gram >= kGramPadded) {
+      geo = plain;
+      geo.pitch = geo.sl + kGramPad;
+      geo.stage_bytes = rows * geo.pitch * esize;
+      geo.gram_mma = kGramPadded;
+      ok = ring_stage(geo, warp_cap(bwd, n), T, num_sms);
+    }
+    if (!ok) geo = plain;
   }
   if (bwd) {
     const int cap = bwd_warp_cap(n, bwd_blocked(n, proj, geo.ns));
@@ -1750,6 +1857,31 @@ inline void ring_tensor_maps(WarpGeometry& geo, RingMaps& maps, const void* cons
   geo.tma = 1;
 }
 
+// Tensor maps of the swizzled tensor-core Gram stages (kGramSwizzled): the
+// plain ring's view [T * rows[k]][D / 64][64] and box [rows[k]][sl / 64][64],
+// with the 128-byte swizzle; a slice lands in the tensor's 1024-byte aligned
+// region (gram_mma_slice). False when a map cannot be encoded.
+inline bool ring_tensor_maps_swz(const WarpGeometry& geo, RingMaps& maps, const void* const* base, const int* rows,
+                                 int nin, int64_t T, int64_t D, int esize) {
+  if (esize != 2 || D % kTmaChunk != 0 || geo.sl % kTmaChunk != 0 || nin > 4) return false;
+  const auto encode = tensor_map_encoder();
+  if (!encode) return false;
+  for (int k = 0; k < nin; ++k) {
+    if (T * rows[k] >= (int64_t(1) << 31)) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kTmaChunk), static_cast<cuuint64_t>(D / kTmaChunk),
+                                static_cast<cuuint64_t>(T * rows[k])};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kTmaChunk) * esize, static_cast<cuuint64_t>(D) * esize};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTmaChunk), static_cast<cuuint32_t>(geo.sl / kTmaChunk),
+                               static_cast<cuuint32_t>(rows[k])};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode(&maps.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base[k]), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
+}
+
 template <typename KernelT>
 inline int warp_prepare(KernelT* kernel, int smem_bytes) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
@@ -1789,10 +1921,10 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, 
   return launch_status();
 }
 
-template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK, bool MMA = false>
+template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK, bool MMA = false, bool SWZ = false>
 int launch_bwd_kernel(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
                       cudaStream_t s) {
-  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK, MMA>;
+  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK, MMA, SWZ>;
   if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
   return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps);
 }
@@ -1803,9 +1935,13 @@ template <typename T, typename P, int N, bool FUSED, bool PROJ>
 int launch_bwd_blocked(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
                        cudaStream_t s) {
   if constexpr (gram_mma_dtype(sizeof(T))) {
-    if (geo.gram_mma) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true, true>(geo, maps, block, a, s);
+    if constexpr (N % 2 == 0) {  // the geometry takes swizzled stages for even n only
+      if (geo.gram_mma == kGramSwizzled)
+        return launch_bwd_kernel<T, P, N, FUSED, PROJ, true, true, true>(geo, maps, block, a, s);
+    }
+    if (geo.gram_mma == kGramPadded) return launch_bwd_kernel<T, P, N, FUSED, PROJ, true, true>(geo, maps, block, a, s);
   }
-  if (geo.gram_mma) return HC_ERR_LAUNCH;  // not reached: the geometry pads only half-precision rings
+  if (geo.gram_mma) return HC_ERR_LAUNCH;  // not reached: only half-precision rings take the tensor-core Gram
   return launch_bwd_kernel<T, P, N, FUSED, PROJ, true>(geo, maps, block, a, s);
 }
 
@@ -1824,13 +1960,20 @@ int launch_bwd_one(const WarpGeometry& geo, const RingMaps& maps, dim3 block, co
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_bwd_warp(int n, const WarpGeometry& geo_in, const MixBwdArgs& a, cudaStream_t s) {
   WarpGeometry geo = geo_in;
-  geo.status = timeout_word(s);
   RingMaps maps;
   {
     const void* base[4] = {a.g, a.x, a.gu, a.f};
     const int rows[4] = {n, n, 1, 1};
-    ring_tensor_maps(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T));
+    if (geo.gram_mma == kGramSwizzled) {
+      if (ring_tensor_maps_swz(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T))) {
+        geo.tma = 1;
+      } else if (!warp_geometry(geo, true, FUSED, PROJ, n, a.T, a.D, sizeof(T), sm_count(), kGramPadded)) {
+        return HC_ERR_LAUNCH;  // no swizzled maps: padded rows copied one by one
+      }
+    }
+    if (geo.gram_mma != kGramSwizzled) ring_tensor_maps(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T));
   }
+  geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
