@@ -40,8 +40,17 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
   const int es = dtype_size(sdt);
   if (!streams_aligned || !rw_ring_supported(n, m) || D % (16 / es) != 0) return false;
   const int cap = rw_cap(bwd, n, m, mixw, proj);
-  if (!ring_geometry(geo, rw_rows(bwd, n, m, mixw), cap, T, D, es, sm_count(), bwd)) return false;
-  if (bwd && cap > 8) prefer_bwd_consumers(geo, 4);  // the read / mix-write caps exceed 8 only for small tokens
+  const int rows = rw_rows(bwd, n, m, mixw);
+  if (!ring_geometry(geo, rows, cap, T, D, es, sm_count(), bwd)) return false;
+  if (bwd && geo.ns > 1 && rw_gram_mma(n, mixw, es)) {
+    // the Gram on the tensor cores, ring rows padded by 16 bytes (rw_gram_finish)
+    const WarpGeometry plain = geo;
+    geo.pitch = geo.sl + kGramPad;
+    geo.stage_bytes = rows * geo.pitch * es;
+    geo.gram_mma = kGramPadded;
+    if (!ring_stage(geo, kRwMmaWarps, T, sm_count())) geo = plain;
+  }
+  if (bwd && (cap > 8 || geo.gram_mma)) prefer_bwd_consumers(geo, 4);
   if (mixw) prefer_producers(geo);
   return true;
 }

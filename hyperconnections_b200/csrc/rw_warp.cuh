@@ -401,11 +401,150 @@ __device__ __forceinline__ void rw_bwd_finish(const RwArgs& a, const RwParams<N,
   }
 }
 
-template <typename T, int N, int M, bool MIXW, bool PROJ>
-__global__ void __launch_bounds__(rw_bwd_cap(N, M, MIXW, PROJ) * 32, 1)
+// ------------------------------------ mix-write backward, Gram on the tensor cores
+// Half-precision streams cut into slices at n >= 5: the consumer computes
+// grad_x and grad_f of each slice on the CUDA cores (rw_bwd_grads_slice, no
+// sums) and the token's Gram M = G [X; F]^T (N x (N + M), g rows against the
+// x and f rows) on the tensor cores (gram_mma_slice, ring rows padded by 16
+// bytes); every parameter gradient then follows from M (rw_gram_finish):
+//   grad_H_ij = M_ij [- v_j rho_i],  grad_W_ik = M_i,N+k,
+//   rho_i = sum_d g_i v^T x = sum_j v_j M_ij,  bp_j = sum_d (c^T g) x_j = sum_i c_i M_ij,
+//   grad_v_j = rho_j - sum_i H_ij rho_i + bp_j (ops/stream_mix_small_nb.py:379-384).
+constexpr bool rw_gram_mma(int n, bool mixw, int esize) { return mixw && n >= 5 && gram_mma_dtype(esize); }
+// 8 warps (7 consumers, the count sliced backward rings run): H, W, v and c
+// stay in registers (up to 112 floats at n = 8, m = 4), 255 registers a thread.
+constexpr int kRwMmaWarps = 8;
+
+template <typename T, int N, int M, bool PROJ, int W>
+__device__ __forceinline__ void rw_bwd_grads_slice(const RwArgs& a, const RwParams<N, M, true, PROJ>& pr,
+                                                   const uint8_t* gsb, int pitch, int64_t t, int64_t d0, int len,
+                                                   int lane) {
+  using Wd = Word<T>;
+  constexpr int K = Wd::K;
+  constexpr int es = sizeof(T);
+  constexpr int SEGW = 32 * W * K;
+  const int64_t D = a.D;
+  const uint32_t rowb = static_cast<uint32_t>(pitch) * es;
+  T* gxt = a.grad_x ? static_cast<T*>(a.grad_x) + t * N * D + d0 : nullptr;
+  T* gft = a.grad_f ? static_cast<T*>(a.grad_f) + t * M * D + d0 : nullptr;
+  if (gxt == nullptr && gft == nullptr) return;
+  for (int e0 = lane * W * K; e0 < len; e0 += SEGW) {
+    const uint32_t eo = static_cast<uint32_t>(e0) * es;
+    Words<W> gw[N];
+#pragma unroll
+    for (int r = 0; r < N; ++r) gw[r] = lds_words<W>(gsb + eo + r * rowb);
+    uint32_t gxo[N][W], gfo[M][W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float ge[N][K];
+#pragma unroll
+      for (int r = 0; r < N; ++r) Wd::get(gw[r].w[w], ge[r]);
+      float bt[K];  // c^T g per element (projection)
+      if constexpr (PROJ) {
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float b = 0.f;
+#pragma unroll
+          for (int i = 0; i < N; ++i) b = fmaf(ge[i][e], pr.cc[i], b);
+          bt[e] = b;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float s = 0.f;
+#pragma unroll
+          for (int r = 0; r < N; ++r) s = fmaf(pr.a[r * N + j], ge[r][e], s);
+          if constexpr (PROJ) s = fmaf(pr.vv[j], bt[e], s);
+          o[e] = s;
+        }
+        gxo[j][w] = Wd::put(o);
+      }
+#pragma unroll
+      for (int k = 0; k < M; ++k) {
+        float o[K];
+#pragma unroll
+        for (int e = 0; e < K; ++e) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < N; ++i) s = fmaf(pr.w[i * M + k], ge[i][e], s);
+          o[e] = s;
+        }
+        gfo[k][w] = Wd::put(o);
+      }
+    }
+    if (gxt) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) stg_words<W>(gxt + j * D + e0, gxo[j]);
+    }
+    if (gft) {
+#pragma unroll
+      for (int k = 0; k < M; ++k) stg_words<W>(gft + k * D + e0, gfo[k]);
+    }
+  }
+}
+
+// The token's parameter gradients from its Gram M (row-major N x (N + M) in
+// shared memory); lane i < N handles row i of grad_H and grad_W and entry i of
+// grad_v. Register arrays are indexed with constants only.
+template <int N, int M, bool PROJ>
+__device__ __forceinline__ void rw_gram_finish(const RwArgs& a, const RwParams<N, M, true, PROJ>& pr,
+                                               const float* gram, int64_t t, int lane) {
+  constexpr int C = N + M;
+  const int i = lane < N ? lane : 0;
+  const float* row = gram + i * C;
+  float rho = 0.f, bp = 0.f;
+  if constexpr (PROJ) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) rho = fmaf(pr.vv[j], row[j], rho);
+#pragma unroll
+    for (int q = 0; q < N; ++q) bp = fmaf(pr.cc[q], gram[q * C + i], bp);  // column i
+  }
+  float rho_all[PROJ ? N : 1];
+  if constexpr (PROJ) {
+#pragma unroll
+    for (int q = 0; q < N; ++q) rho_all[q] = __shfl_sync(kFull, rho, q);
+  }
+  if (lane < N) {
+    if (a.grad_H) {
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float h = row[j];
+        if constexpr (PROJ) h = fmaf(-pr.vv[j], rho, h);
+        a.grad_H[t * (N * N) + i * N + j] = h;
+      }
+    }
+    if (a.grad_W) {
+#pragma unroll
+      for (int k = 0; k < M; ++k) a.grad_W[t * (N * M) + i * M + k] = row[N + k];
+    }
+    if constexpr (PROJ) {
+      if (a.grad_v) {
+        float ht = 0.f;  // sum_q H_q,i rho_q, column i of H with a constant index
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          if (j == i) {
+#pragma unroll
+            for (int q = 0; q < N; ++q) ht = fmaf(pr.a[q * N + j], rho_all[q], ht);
+          }
+        }
+        a.grad_v[t * N + i] = (rho - ht) + bp;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+template <typename T, int N, int M, bool MIXW, bool PROJ, bool MMA = false>
+__global__ void __launch_bounds__((MMA ? kRwMmaWarps : rw_bwd_cap(N, M, MIXW, PROJ)) * 32, 1)
 rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
+  static_assert(!MMA || (MIXW && sizeof(T) == 2), "the tensor-core Gram is a mix-write, half-precision path");
   using L = RwLayout<N, M, MIXW, PROJ>;
-  constexpr int W = rw_bwd_words(N, M, MIXW, PROJ);
+  constexpr int W = MMA ? 2 : rw_bwd_words(N, M, MIXW, PROJ);
+  constexpr int NT = (N + M + 7) / 8;
+  __shared__ float gram_all[MMA ? (kWarpMaxWarps - 1) * N * (N + M) : 1];
   constexpr int es = sizeof(T);
   constexpr int NG = MIXW ? N : M;
   constexpr int NIN = MIXW ? 3 : 2;
@@ -434,7 +573,9 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   } else if (warp - 1 < C) {
     const int c = warp - 1;
     RwParams<N, M, MIXW, PROJ> pr;
-    float acc[L::kPad];
+    float acc[MMA ? 1 : L::kPad];
+    float cg[MMA ? NT : 1][4];  // tensor-core Gram accumulators of the token
+    float* gram = gram_all + (MMA ? c * N * (N + M) : 0);
     RingCursor cur{c, 0u, c};
     for (int g0 = 0; g0 < nunits; g0 += C) {
       const int Wg = min(C, nunits - g0);
@@ -460,12 +601,29 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
           const int64_t t = t0 + tt;
           if (p == 0) {
             if (tt > 0) pr.load(a, t);
+            if constexpr (MMA) {
 #pragma unroll
-            for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+              for (int k = 0; k < NT; ++k) cg[k][0] = cg[k][1] = cg[k][2] = cg[k][3] = 0.f;
+            } else {
+#pragma unroll
+              for (int k = 0; k < L::kPad; ++k) acc[k] = 0.f;
+            }
           }
-          rw_bwd_slice<T, N, M, MIXW, PROJ, W>(a, pr, acc, sb + tt * NG * rowb, sb + greg + tt * N * rowb,
-                                               sb + greg + xreg + tt * M * rowb, geo.pitch, t, d0, len, lane);
-          if (p == ns - 1) rw_bwd_finish<N, M, MIXW, PROJ>(a, pr, acc, t, lane);  // token complete
+          const uint8_t* gs = sb + tt * NG * rowb;
+          const uint8_t* xs = sb + greg + tt * N * rowb;
+          const uint8_t* fs = sb + greg + xreg + tt * M * rowb;
+          if constexpr (MMA) {
+            rw_bwd_grads_slice<T, N, M, PROJ, W>(a, pr, gs, geo.pitch, t, d0, len, lane);
+            gram_mma_slice<T, N, 0, N, M, false>(cg, gs, nullptr, xs, fs, reinterpret_cast<const uint8_t*>(st.zrow),
+                                                 rowb, 0, len, lane);
+            if (p == ns - 1) {  // token complete
+              gram_mma_store<N, N + M>(gram, cg, lane);
+              rw_gram_finish<N, M, PROJ>(a, pr, gram, t, lane);
+            }
+          } else {
+            rw_bwd_slice<T, N, M, MIXW, PROJ, W>(a, pr, acc, gs, xs, fs, geo.pitch, t, d0, len, lane);
+            if (p == ns - 1) rw_bwd_finish<N, M, MIXW, PROJ>(a, pr, acc, t, lane);  // token complete
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&st.empty[cur.s]);
@@ -644,6 +802,14 @@ int rw_launch_one(const WarpGeometry& geo_in, const RwArgs& a, cudaStream_t s) {
   geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   if constexpr (BWD) {
+    if constexpr (rw_gram_mma(N, MIXW, sizeof(T))) {
+      if (geo.gram_mma) {
+        auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ, true>;
+        if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
+        return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
+      }
+    }
+    if (geo.gram_mma) return HC_ERR_LAUNCH;  // not reached: the geometry sets it only for this path
     auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ>;
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
     return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);

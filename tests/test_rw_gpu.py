@@ -155,6 +155,18 @@ def test_sliced_tokens(n, m, D):
     check_all(*inputs(64, n, m, D, torch.bfloat16, n == 4, seed=13), 2e-2, False)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,m,D,proj", [(5, 1, 2048, True), (5, 4, 1800, False), (6, 3, 1024, True),
+                                        (7, 2, 1536, True), (8, 4, 1024, False), (8, 4, 1800, True),
+                                        (8, 2, 2048, True)])
+def test_mix_write_sliced_gram(dtype, n, m, D, proj):
+    """Half-precision tokens cut into slices at n >= 5: the mix-write
+    backward takes its Gram on the tensor cores (ring rows padded, copied row
+    by row); D = 1800 leaves a last slice that is not a multiple of 16
+    elements."""
+    check_all(*inputs(150, n, m, D, dtype, proj, seed=17 * n + m + D), 2e-2, False)
+
+
 @pytest.mark.parametrize("n,m,D", [(2, 1, 1), (4, 2, 7), (4, 4, 2), (6, 3, 33), (3, 1, 100), (2, 4, 16)])
 def test_element_wise_path(n, m, D):
     """Odd or tiny block sizes, and m > n, run the element-wise kernels."""
