@@ -1748,23 +1748,33 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
                           int esize, int num_sms, int max_gram = kGramSwizzled) {
   const int rows = warp_rows(bwd, fused, n);
   if (!ring_geometry(geo, rows, warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
-  if (bwd && geo.ns > 1 && bwd_blocked(n, proj, geo.ns) && gram_mma_dtype(esize)) {
+  // whole tokens, one a stage, at n = 8 (whose single pass holds every sum in
+  // registers at 8 warps): the blocked path on swizzled stages of at most
+  // 24 KB. Measured on B200 (fused backward, bf16, 16,384 tokens): n = 8,
+  // D = 512 (22.5 KB stages) 99.8 against 116.0 us; larger stages leave too
+  // few consumers (n = 8, D = 640, 26.6 KB: 160.7 against 146.3 us), and at
+  // n = 6 the single pass at 12 warps is as fast or faster (D = 768: 124.1
+  // against 108.6 us).
+  constexpr int kWholeMmaMaxStage = 24 * 1024;
+  const bool whole = geo.ns == 1 && geo.tpi == 1 && n == 8;
+  if (bwd && gram_mma_dtype(esize) && ((geo.ns > 1 && bwd_blocked(n, proj, geo.ns)) || whole)) {
     // the tensor-core Gram (gram_mma_slice), on swizzled stages for even
     // n and on padded rows for odd n (measured)
     const WarpGeometry plain = geo;
     bool ok = false;
     if (max_gram >= kGramSwizzled && n % 2 == 0 && D % kTmaChunk == 0 && T * n < (int64_t(1) << 31)) {
       if ((geo.sl / kTmaChunk) % 2 == 0) {  // an odd number of 128-byte lines a row
-        geo.sl += kTmaChunk;
+        geo.sl += kTmaChunk;                // (a whole token's box then ends in a zero-filled chunk)
         geo.pitch = geo.sl;
         geo.ns = static_cast<int>((D + geo.sl - 1) / geo.sl);
       }
       geo.stage_bytes =
           2 * swz_region_bytes(n, geo.sl, esize) + (fused ? 2 * swz_region_bytes(1, geo.sl, esize) : 0);
       geo.gram_mma = kGramSwizzled;
-      ok = geo.ns > 1 && ring_stage(geo, warp_cap(bwd, n), T, num_sms, kSwzAlign);
+      ok = (plain.ns > 1 ? geo.ns > 1 : geo.stage_bytes <= kWholeMmaMaxStage) &&
+           ring_stage(geo, warp_cap(bwd, n), T, num_sms, kSwzAlign);
     }
-    if (!ok && max_gram >= kGramPadded) {
+    if (!ok && max_gram >= kGramPadded && plain.ns > 1) {  // padded rows: slices, copied row by row
       geo = plain;
       geo.pitch = geo.sl + kGramPad;
       geo.stage_bytes = rows * geo.pitch * esize;
@@ -1774,7 +1784,7 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
     if (!ok) geo = plain;
   }
   if (bwd) {
-    const int cap = bwd_warp_cap(n, bwd_blocked(n, proj, geo.ns));
+    const int cap = bwd_warp_cap(n, bwd_blocked(n, proj, geo.ns) || geo.gram_mma);
     geo.consumers = std::min(geo.consumers, cap - 1);
     if (cap > 8) prefer_bwd_consumers(geo, n);
     prefer_producers(geo);
@@ -1951,7 +1961,7 @@ int launch_bwd_one(const WarpGeometry& geo, const RingMaps& maps, dim3 block, co
     return launch_bwd_blocked<T, P, N, FUSED, PROJ>(geo, maps, block, a, s);
   } else {
     if constexpr (bwd_blocked_n(N)) {
-      if (geo.ns > 1) return launch_bwd_blocked<T, P, N, FUSED, PROJ>(geo, maps, block, a, s);
+      if (geo.ns > 1 || geo.gram_mma) return launch_bwd_blocked<T, P, N, FUSED, PROJ>(geo, maps, block, a, s);
     }
     return launch_bwd_kernel<T, P, N, FUSED, PROJ, false>(geo, maps, block, a, s);
   }

@@ -106,12 +106,14 @@ def test_fused_half(dtype, n, D):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("n", [5, 6, 7, 8])
-@pytest.mark.parametrize("D", [1536, 1800])
+@pytest.mark.parametrize("D", [512, 640, 1536, 1800])
 def test_fused_half_sliced_gram(dtype, n, D):
-    """Tokens cut into slices at n >= 5 with half-precision streams: the
-    blocked backward with its Gram on the tensor cores (ring rows padded,
-    copied row by row). At D = 1800 the last slice is not a multiple of 16
-    elements (its last k-step reads the zero row)."""
+    """Half-precision streams at n >= 5: the blocked backward with its Gram on
+    the tensor cores, on swizzled TMA stages (even n, D a multiple of 64:
+    slices at D = 1536, and whole tokens at n = 8, D = 512 whose box ends in
+    a zero-filled chunk) or 16-byte padded rows (slices at odd n or D = 1800,
+    whose last slice is not a multiple of 16 elements); the other whole
+    tokens keep the single pass."""
     inputs = workload(23, n, D, dtype, seed=11 * n + D)
     u, x_out, grads = run(*inputs)
     check(u, x_out, grads, inputs, None, rel=False)

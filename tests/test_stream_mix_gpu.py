@@ -265,7 +265,8 @@ def test_golden_reference_triton_fp16(case):
 
 
 @pytest.mark.parametrize("B,N,D,proj", [(3000, 4, 1024, True), (5000, 2, 2048, False), (800, 8, 4096, True),
-                                        (300, 5, 2400, True), (300, 7, 1800, True), (300, 6, 1800, False)])
+                                        (300, 5, 2400, True), (300, 7, 1800, True), (300, 6, 1800, False),
+                                        (300, 6, 512, True), (300, 8, 640, True), (300, 8, 1536, False)])
 def test_many_tokens_per_cta(B, N, D, proj):
     """The pipelined kernels with many tokens per CTA, bf16 streams, repeated
     launches: forward and backward against the oracle."""
