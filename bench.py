@@ -884,9 +884,9 @@ class RwRunner:
                                               self.stream), "hc_mix_write_bwd")
 
 
-def time_launches(device, fns, steps, warmup):
+def time_launches(device, fns, steps, warmup, flush_mode="clean"):
     """Mean device ms of each callable in `fns`, L2 flushed between steps."""
-    flush = L2Flush(device)
+    flush = L2Flush(device, flush_mode)
     for _ in range(warmup):
         for fn in fns:
             fn()
@@ -982,7 +982,7 @@ def time_stream_mix(device, B, N, D, dtype, proj, steps, warmup):
         _lib.check(lib.hc_stream_mix_bwd(G.data_ptr(), Phi.data_ptr(), x.data_ptr(), _lib.ptr(v), gx.data_ptr(),
                                          gP.data_ptr(), _lib.ptr(gv), B, N, D, code, code, st), "hc_stream_mix_bwd")
 
-    return time_launches(device, [fwd, bwd], steps, warmup)
+    return time_launches(device, [fwd, bwd], steps, warmup, flush_mode="write")
 
 
 def time_pade(device, B, n, steps, warmup):

@@ -1,6 +1,6 @@
 // bign_inst.cuh — instantiates the n > 8 stream_mix_add kernels for one stream
 // dtype. Included by bign_<dtype>.cu with HC_T, HC_SUFFIX and HC_T_IS_F32.
-#include "bign.cuh"
+#include "bign_ring.cuh"
 
 #define HC_CAT2(a, b) a##b
 #define HC_CAT(a, b) HC_CAT2(a, b)
@@ -12,8 +12,13 @@ int big_fwd_p(bool proj, bool vec, int n, const MixFwdArgs& a, cudaStream_t s) {
   if (proj) return vec ? launch_big_fwd<T, P, true, true>(n, a, s) : launch_big_fwd<T, P, true, false>(n, a, s);
   return vec ? launch_big_fwd<T, P, false, true>(n, a, s) : launch_big_fwd<T, P, false, false>(n, a, s);
 }
+// Half-precision streams with D a multiple of 64 and aligned rows take the
+// ring kernel on the tensor cores (bign_ring.cuh); every other shape the
+// one-CTA-per-token kernel (bign.cuh).
 template <typename T, typename P>
 int big_bwd_p(bool proj, int n, const MixBwdArgs& a, cudaStream_t s) {
+  const int rc = proj ? launch_big_bwd_ring<T, P, true>(n, a, s) : launch_big_bwd_ring<T, P, false>(n, a, s);
+  if (rc != HC_ERR_UNSUPPORTED_N) return rc;
   return proj ? launch_big_bwd<T, P, true, false>(n, a, s) : launch_big_bwd<T, P, false, false>(n, a, s);
 }
 }  // namespace

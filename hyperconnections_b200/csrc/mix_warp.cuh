@@ -1321,6 +1321,7 @@ constexpr bool gram_mma_dtype(int esize) { return HC_GRAM_MMA && esize == 2; }
 constexpr int kGramPadded = 1;    // geo.gram_mma: row copies into 16-byte padded rows
 constexpr int kGramSwizzled = 2;  // geo.gram_mma: swizzled TMA tensor copies
 constexpr int kGramPad = 8;       // elements of padding per row of kGramPadded stages
+constexpr int kGramBudget = 216 * 1024;  // bytes of ring stages of the tensor-core Gram backward
 
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
@@ -1653,9 +1654,9 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 //     one bulk copy per tensor moves several tokens.
 // Stages, consumers and shared memory of the ring for geo.stage_bytes; false
 // when fewer than 3 stages (or no consumer) fit.
-inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms, int slack_bytes = 0) {
+inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms, int slack_bytes = 0,
+                       int budget = 200 * 1024) {
   const MixTuning tune = mix_tuning();
-  const int budget = 200 * 1024;
   int stages = std::min<int>(kRingMaxStages, budget / geo.stage_bytes);
   if (tune.stages > 0) stages = std::min(stages, tune.stages);
   int consumers = std::min(warp_cap_ - 1, stages - 2);
@@ -1758,23 +1759,44 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
   constexpr int kWholeMmaMaxStage = 24 * 1024;
   const bool whole = geo.ns == 1 && geo.tpi == 1 && n == 8;
   if (bwd && gram_mma_dtype(esize) && ((geo.ns > 1 && bwd_blocked(n, proj, geo.ns)) || whole)) {
-    // the tensor-core Gram (gram_mma_slice), on swizzled stages for even
-    // n and on padded rows for odd n (measured)
+    // The tensor-core Gram (gram_mma_slice), on swizzled stages for even n
+    // and on padded rows for odd n (measured). The swizzled rings take
+    // kGramBudget of stages, sliced so that 9 stages fit: 7 consumers each
+    // holding one and two loading (n = 6, D = 4096: 503 against 571 us with 8
+    // stages of 24.5 KB; n = 8, D = 2048 with 22 KB instead of 26 KB stages:
+    // 358 against 456 us; n = 8, D = 4096: 697 against 890 us).
     const WarpGeometry plain = geo;
+    const MixTuning tune = mix_tuning();
+    int cap = kGramBudget / 9;
+    if (tune.stage_bytes > 0) cap = std::min(cap, static_cast<int>(tune.stage_bytes));
     bool ok = false;
     if (max_gram >= kGramSwizzled && n % 2 == 0 && D % kTmaChunk == 0 && T * n < (int64_t(1) << 31)) {
-      if ((geo.sl / kTmaChunk) % 2 == 0) {  // an odd number of 128-byte lines a row
-        geo.sl += kTmaChunk;                // (a whole token's box then ends in a zero-filled chunk)
-        geo.pitch = geo.sl;
-        geo.ns = static_cast<int>((D + geo.sl - 1) / geo.sl);
+      const auto stage_of = [&](int nc) {
+        return 2 * swz_region_bytes(n, nc * kTmaChunk, esize) +
+               (fused ? 2 * swz_region_bytes(1, nc * kTmaChunk, esize) : 0);
+      };
+      const int64_t chunks = D / kTmaChunk;
+      int nc;
+      if (plain.ns == 1) {  // the whole token: its chunks, odd (the box's last one zero-filled)
+        nc = static_cast<int>(chunks) | 1;
+      } else {  // an odd number of 128-byte lines a row, as evenly split as that allows
+        int nc_max = 1;
+        for (int c2 = 3; c2 <= 255 && stage_of(c2) <= cap; c2 += 2) nc_max = c2;
+        const int64_t ns = (chunks + nc_max - 1) / nc_max;
+        nc = static_cast<int>((chunks + ns - 1) / ns) | 1;
       }
-      geo.stage_bytes =
-          2 * swz_region_bytes(n, geo.sl, esize) + (fused ? 2 * swz_region_bytes(1, geo.sl, esize) : 0);
+      geo.sl = nc * kTmaChunk;
+      geo.pitch = geo.sl;
+      geo.ns = static_cast<int>((D + geo.sl - 1) / geo.sl);
+      geo.stage_bytes = stage_of(nc);
       geo.gram_mma = kGramSwizzled;
       ok = (plain.ns > 1 ? geo.ns > 1 : geo.stage_bytes <= kWholeMmaMaxStage) &&
-           ring_stage(geo, warp_cap(bwd, n), T, num_sms, kSwzAlign);
+           ring_stage(geo, warp_cap(bwd, n), T, num_sms, kSwzAlign, kGramBudget);
     }
-    if (!ok && max_gram >= kGramPadded && plain.ns > 1) {  // padded rows: slices, copied row by row
+    if (!ok && max_gram >= kGramPadded && plain.ns > 1) {
+      // padded rows: the plain ring's slices, copied row by row (re-sliced
+      // for 9 stages of a 216 KB ring, n = 7, D = 1536 measured 289 against
+      // 250 us, and n = 5, D = 2048 242 against 231 us)
       geo = plain;
       geo.pitch = geo.sl + kGramPad;
       geo.stage_bytes = rows * geo.pitch * esize;
@@ -1909,12 +1931,10 @@ template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, cudaStream_t s) {
   WarpGeometry geo = geo_in;
   geo.status = timeout_word(s);
-  RingMaps maps;
-  {
-    const void* base[2] = {a.x, a.src};
-    const int rows[2] = {n, FUSED ? 1 : n};
-    ring_tensor_maps(geo, maps, base, rows, 2, a.T, a.D, sizeof(T));
-  }
+  // The forward copies slices row by row: TMA tensor copies measured no
+  // faster on B200 (n = 4, 6, 8, D = 1024..2048, within 1-2%).
+  RingMaps maps{};
+  geo.tma = 0;
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   switch (n) {
 #define HC_CASE(NN)                                                     \
@@ -1970,7 +1990,7 @@ int launch_bwd_one(const WarpGeometry& geo, const RingMaps& maps, dim3 block, co
 template <typename T, typename P, bool FUSED, bool PROJ>
 int launch_mix_bwd_warp(int n, const WarpGeometry& geo_in, const MixBwdArgs& a, cudaStream_t s) {
   WarpGeometry geo = geo_in;
-  RingMaps maps;
+  RingMaps maps{};
   {
     const void* base[4] = {a.g, a.x, a.gu, a.f};
     const int rows[4] = {n, n, 1, 1};
@@ -1981,7 +2001,11 @@ int launch_mix_bwd_warp(int n, const WarpGeometry& geo_in, const MixBwdArgs& a, 
         return HC_ERR_LAUNCH;  // no swizzled maps: padded rows copied one by one
       }
     }
-    if (geo.gram_mma != kGramSwizzled) ring_tensor_maps(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T));
+    // Plain TMA slices only for the blocked backward with the CUDA-core Gram
+    // (fp32 streams): measured on B200, +7-11% there (n = 6, 8, D = 1024),
+    // but 7-9% slower than row copies for the single pass (n = 4, D = 2048).
+    if (geo.gram_mma == 0 && geo.ns > 1 && bwd_blocked(n, PROJ, geo.ns))
+      ring_tensor_maps(geo, maps, base, rows, FUSED ? 4 : 2, a.T, a.D, sizeof(T));
   }
   geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);

@@ -1,4 +1,5 @@
-"""GPU parity of stream_mix_add for 9 <= N <= 32 (the shared-memory kernels),
+"""GPU parity of stream_mix_add for 9 <= N <= 32 (the shared-memory kernels,
+and the ring kernel on the tensor cores for half-precision streams),
 against the reference's small-NB Function run on CPU (tests/golden/
 stream_mix_large_n.npz) and the float64 oracle. Tolerances as for N <= 8:
 1e-5 relative in fp32; 2e-2 (bf16) / 1e-2 (fp16) absolute wherever |ref| < 8,
@@ -107,6 +108,26 @@ def test_half(N, dtype, phi_dtype):
     pd = torch.float32 if phi_dtype == "f32" else dtype
     check(*inputs(6, N, 1024, dtype, True, seed=N, phi_dtype=pd), half_streams=True)
     check(*inputs(6, N, 1030, dtype, False, seed=N + 1, phi_dtype=pd), half_streams=True)
+
+
+@pytest.mark.parametrize("N", [9, 17, 24, 32])
+@pytest.mark.parametrize("D", [64, 192, 1536])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_half_ring(N, D, dtype):
+    """Half-precision streams with D a multiple of 64: the ring kernel with
+    grad_x and the Gram on the tensor cores (whole tokens and slices, Phi in
+    fp32 and in the stream dtype, with and without the projection)."""
+    check(*inputs(40, N, D, dtype, N % 2 == 1, seed=N * 31 + D), half_streams=True)
+    check(*inputs(40, N, D, dtype, N % 2 == 0, seed=N * 37 + D, phi_dtype=dtype), half_streams=True)
+
+
+def test_half_ring_many_tokens():
+    """Many tokens per CTA: every consumer cycles the ring many times."""
+    from hyperconnections_b200 import _lib
+
+    for _ in range(2):
+        check(*inputs(900, 24, 640, torch.bfloat16, True, seed=5), half_streams=True)
+    assert _lib.wait_timeouts() == 0
 
 
 def test_odd_alignment_views():
