@@ -7,14 +7,16 @@
 
 namespace hc {
 namespace {
+// Half-precision streams with D a multiple of 64 and aligned rows take the
+// ring kernels on the tensor cores (bign_ring.cuh); every other shape the
+// one-CTA-per-token kernels (bign.cuh).
 template <typename T, typename P>
 int big_fwd_p(bool proj, bool vec, int n, const MixFwdArgs& a, cudaStream_t s) {
+  const int rc = proj ? launch_big_fwd_ring<T, P, true>(n, a, s) : launch_big_fwd_ring<T, P, false>(n, a, s);
+  if (rc != HC_ERR_UNSUPPORTED_N) return rc;
   if (proj) return vec ? launch_big_fwd<T, P, true, true>(n, a, s) : launch_big_fwd<T, P, true, false>(n, a, s);
   return vec ? launch_big_fwd<T, P, false, true>(n, a, s) : launch_big_fwd<T, P, false, false>(n, a, s);
 }
-// Half-precision streams with D a multiple of 64 and aligned rows take the
-// ring kernel on the tensor cores (bign_ring.cuh); every other shape the
-// one-CTA-per-token kernel (bign.cuh).
 template <typename T, typename P>
 int big_bwd_p(bool proj, int n, const MixBwdArgs& a, cudaStream_t s) {
   const int rc = proj ? launch_big_bwd_ring<T, P, true>(n, a, s) : launch_big_bwd_ring<T, P, false>(n, a, s);

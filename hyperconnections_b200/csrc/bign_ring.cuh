@@ -1,6 +1,6 @@
-// bign_ring.cuh — stream_mix_add backward for 9 <= n <= 32 streams with
-// half-precision streams, on the shared-memory ring of mix_warp.cuh and the
-// tensor cores.
+// bign_ring.cuh — stream_mix_add for 9 <= n <= 32 streams with
+// half-precision streams, backward and forward, on the shared-memory ring of
+// mix_warp.cuh and the tensor cores.
 //
 // Same arithmetic as big_bwd_kernel (bign.cuh; reference
 // ops/stream_mix_small_nb.py:341-391 and stream_mix_big_nb.py for N >= 16):
@@ -78,13 +78,15 @@ struct BigTokA {
 // Phi'^T: register r of tile (mt, ks) holds rows j = 16 mt + lane / 4 (+8 for
 // r odd) and columns i = 16 ks + 2 (lane % 4) (+8 for r >= 2), two columns a
 // word. vs / cs: the warp's v and c (NMAX floats each, zero past n).
-template <typename T, typename P, int NMAX, bool PROJ>
-__device__ __forceinline__ void big_tok_load(const MixBwdArgs& a, int64_t t, int n, BigTokA<NMAX>& A, float* vs,
-                                             float* cs, int lane) {
+// (TRANS = false: the A fragments of Phi' itself, rows i and columns j, for
+// the forward.)
+template <typename T, typename P, int NMAX, bool PROJ, bool TRANS = true>
+__device__ __forceinline__ void big_tok_load(const void* phi, const void* v, int64_t t, int n, BigTokA<NMAX>& A,
+                                             float* vs, float* cs, int lane) {
   constexpr int MT = BigMma<NMAX>::MT;
-  const P* ph = static_cast<const P*>(a.phi) + t * n * n;
+  const P* ph = static_cast<const P*>(phi) + t * n * n;
   if constexpr (PROJ) {
-    const P* vp = static_cast<const P*>(a.v) + t * n;
+    const P* vp = static_cast<const P*>(v) + t * n;
     if (lane < NMAX) vs[lane] = lane < n ? Elem<P>::to_f(vp[lane]) : 0.f;
     __syncwarp();
     if (lane < NMAX) {
@@ -102,11 +104,12 @@ __device__ __forceinline__ void big_tok_load(const MixBwdArgs& a, int64_t t, int
     for (int ks = 0; ks < MT; ++ks) {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int j = 16 * mt + g + ((r & 1) ? 8 : 0);
+        const int row = 16 * mt + g + ((r & 1) ? 8 : 0);
         float h[2], l[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int i = 16 * ks + 2 * q + ((r & 2) ? 8 : 0) + e;
+          const int col = 16 * ks + 2 * q + ((r & 2) ? 8 : 0) + e;
+          const int i = TRANS ? col : row, j = TRANS ? row : col;  // Phi'_ij = Phi_ij + c_i v_j
           float val = 0.f;
           if (i < n && j < n) {
             val = Elem<P>::to_f(ph[i * n + j]);
@@ -311,7 +314,7 @@ big_bwd_ring_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
       const int Wg = min(C, ntok - g0);
       if (c >= Wg) break;
       const int64_t t = t_begin + g0 + c;
-      big_tok_load<T, P, NMAX, PROJ>(a, t, n, A, vs, cs, lane);  // overlaps the wait for the data
+      big_tok_load<T, P, NMAX, PROJ>(a.phi, a.v, t, n, A, vs, cs, lane);  // overlaps the wait for the data
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -343,7 +346,122 @@ big_bwd_ring_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
   ring_drain(st, S);
 }
 
-// Ring geometry of the kernel above for n rows of G and of x a token: slices
+// ------------------------------------------------------------------ forward
+// out_i = sum_j Phi'_ij x_j + Y_i (Phi' = Phi [+ c v^T]; reference
+// ops/stream_mix_small_nb.py:75-132): the ring holds a slice of the token's x
+// and Y rows (swizzled stages as above); per 16-element step the consumer
+// loads the x rows transposed as the B operand, multiplies by Phi' (A operand,
+// hi / lo split, registers), adds Y from the stage to the fp32 accumulators
+// and stores out straight from them.
+template <typename T, int NMAX>
+__device__ __forceinline__ void big_fwd_slice(const BigTokA<NMAX>& A, const uint8_t* xs, const uint8_t* ys,
+                                              const uint8_t* zrow, int nc, int n, int len, T* ot, int64_t D,
+                                              int lane) {
+  constexpr int MT = BigMma<NMAX>::MT;
+  constexpr int es = sizeof(T);
+  const int q = lane >> 3;
+  const int g = lane >> 2, qd = lane & 3;
+  const uint32_t z = smem_u32(zrow);
+  const int ar = (q & 1) * 8 + (lane & 7), akof = (q >> 1) * 8;
+  for (int k0 = 0; k0 < len; k0 += 16) {
+    uint32_t xt[MT][4];
+#pragma unroll
+    for (int ks = 0; ks < MT; ++ks) {
+      const int j = 16 * ks + ar;
+      ldsm_x4_trans<T>(xt[ks], j < n ? smem_u32(swz_at(xs, nc, j, (k0 + akof) * es)) : z);
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      float c[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) c[h][0] = c[h][1] = c[h][2] = c[h][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < MT; ++ks) {
+        MmaKind<T>::mma(c[0], A.hi[mt][ks], xt[ks][0], xt[ks][1]);
+        MmaKind<T>::mma(c[0], A.lo[mt][ks], xt[ks][0], xt[ks][1]);
+        MmaKind<T>::mma(c[1], A.hi[mt][ks], xt[ks][2], xt[ks][3]);
+        MmaKind<T>::mma(c[1], A.lo[mt][ks], xt[ks][2], xt[ks][3]);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = k0 + 8 * h + 2 * qd;
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int i = 16 * mt + g + 8 * hr;
+          if (i < n) {
+            float y[2];
+            Word<T>::get(*reinterpret_cast<const uint32_t*>(swz_at(ys, nc, i, col * es)), y);
+            *reinterpret_cast<uint32_t*>(ot + i * D + col) =
+                pack2<T>(c[h][2 * hr] + y[0], c[h][2 * hr + 1] + y[1]);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename T, typename P, int NMAX, bool PROJ>
+__global__ void __launch_bounds__(kBigRingWarps * 32, 1)
+big_fwd_ring_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps, int n) {
+  static_assert(sizeof(T) == 2, "half-precision streams");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* const smem = smem_raw + ((kSwzAlign - (smem_u32(smem_raw) & (kSwzAlign - 1))) & (kSwzAlign - 1));
+  __shared__ RingState st;
+  __shared__ float warp_vec[kBigRingWarps - 1][2][NMAX];  // per consumer: v, c
+  pdl_launch_dependents();
+  ring_init(st, geo.stages);
+  pdl_wait_prior_grid();
+
+  const int64_t T_ = a.T, D = a.D;
+  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
+  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = geo.stages, C = geo.consumers, ns = geo.ns;
+  const int nc = geo.sl / kTmaChunk;
+  const int rn = swz_region_bytes(n, geo.sl, 2);
+
+  if (warp == 0) {
+    if (lane < geo.producers) {
+      const void* base[2] = {a.x, a.src};
+      const int rows[2] = {n, n};
+      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, ntok, base, rows, lane, &maps);
+    }
+  } else if (warp - 1 < C) {
+    const int c = warp - 1;
+    BigTokA<NMAX> A;
+    RingCursor cur{c, 0u, c};
+    for (int g0 = 0; g0 < ntok; g0 += C) {
+      const int Wg = min(C, ntok - g0);
+      if (c >= Wg) break;
+      const int64_t t = t_begin + g0 + c;
+      big_tok_load<T, P, NMAX, PROJ, false>(a.phi, a.v, t, n, A, warp_vec[c][0], warp_vec[c][1], lane);
+      T* ot = static_cast<T*>(a.out) + t * n * D;
+      bool ok = true;
+      for (int p = 0; p < ns; ++p) {
+        if (__any_sync(kFull, st.abort) || !ring_wait_item(st, cur, geo.wait_limit)) {
+          if (lane == 0 && !st.abort) {
+            report_timeout(&g_mix_wait_timeouts, geo.status);
+            st.abort = 1;
+          }
+          ok = false;
+          break;
+        }
+        const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
+        const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
+        const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
+        big_fwd_slice<T, NMAX>(A, sb, sb + rn, reinterpret_cast<const uint8_t*>(st.zrow), nc, n, len, ot + d0, D,
+                               lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st.empty[cur.s]);
+        cur.advance(p + 1 < ns ? Wg : C, S);
+      }
+      if (!ok) break;
+    }
+  }
+  ring_drain(st, S);
+}
+
+// Ring geometry of the kernels above for two tensors of n rows a token: slices
 // of an odd number of 64-element chunks (at most the chunks that let 9 stages
 // fit the ring), split as evenly as that allows; false when the shape does
 // not fit (the caller then runs big_bwd_kernel).
@@ -401,6 +519,39 @@ int launch_big_bwd_ring(int n, const MixBwdArgs& a, cudaStream_t s) {
     geo.tma = 1;
     return n <= 16 ? launch_big_bwd_ring_n<T, P, 16, PROJ>(n, geo, maps, a, s)
                    : launch_big_bwd_ring_n<T, P, 32, PROJ>(n, geo, maps, a, s);
+  }
+}
+
+template <typename T, typename P, int NMAX, bool PROJ>
+int launch_big_fwd_ring_n(int n, const WarpGeometry& geo_in, const RingMaps& maps, const MixFwdArgs& a,
+                          cudaStream_t s) {
+  WarpGeometry geo = geo_in;
+  geo.status = timeout_word(s);
+  auto* k = big_fwd_ring_kernel<T, P, NMAX, PROJ>;
+  if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
+  const dim3 block((geo.consumers + 1) * 32, 1, 1);
+  if (int rc = launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps, n)) return rc;
+  return launch_status();
+}
+
+// The forward ring kernel when the shape and the pointers allow it (returns
+// HC_ERR_UNSUPPORTED_N otherwise, so the caller runs big_fwd_kernel).
+template <typename T, typename P, bool PROJ>
+int launch_big_fwd_ring(int n, const MixFwdArgs& a, cudaStream_t s) {
+  if constexpr (sizeof(T) != 2) {
+    return HC_ERR_UNSUPPORTED_N;
+  } else {
+    WarpGeometry geo;
+    if (!HC_GRAM_MMA || !aligned16(a.x) || !aligned16(a.src) || !aligned4(a.out) ||
+        !big_ring_geometry(geo, n, a.T, a.D))
+      return HC_ERR_UNSUPPORTED_N;
+    RingMaps maps{};
+    const void* base[2] = {a.x, a.src};
+    const int rows[2] = {n, n};
+    if (!ring_tensor_maps_swz(geo, maps, base, rows, 2, a.T, a.D, 2)) return HC_ERR_UNSUPPORTED_N;
+    geo.tma = 1;
+    return n <= 16 ? launch_big_fwd_ring_n<T, P, 16, PROJ>(n, geo, maps, a, s)
+                   : launch_big_fwd_ring_n<T, P, 32, PROJ>(n, geo, maps, a, s);
   }
 }
 
