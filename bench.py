@@ -903,6 +903,22 @@ def time_launches(device, fns, steps, warmup, flush_mode="clean"):
     return [float(np.mean([e[k].elapsed_time(e[k + 1]) for e in evs])) for k in range(len(fns))]
 
 
+# (n, D, projection) of stream_mix_add at 9 <= n <= 32, 2,048 tokens of bf16 streams
+BIG_SWEEP = ((9, 1536, False), (12, 1536, True), (16, 1536, False), (16, 1536, True), (24, 1536, False),
+             (32, 1536, False), (32, 1536, True))
+
+
+def large_n_line(device, N, D, proj, steps, warmup, B=2048):
+    """stream_mix_add forward + backward at 9 <= N <= 32, bf16 streams and
+    Phi (the reference benchmark's dtypes and write flush): GB/s of 3 N D
+    elements a token (+ the N x N fp32 grad_Phi in the backward)."""
+    fwd_ms, bwd_ms = time_stream_mix(device, B, N, D, torch.bfloat16, proj, steps, warmup)
+    nb = 3 * B * N * D * 2
+    return {"sweep": "stream_mix_add_large_n", "tokens": B, "n": N, "D": D, "dtype": "bf16", "proj": proj,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "fwd_gbs": nb / (fwd_ms * 1e-3) / 1e9,
+            "bwd_gbs": (nb + B * N * N * 4) / (bwd_ms * 1e-3) / 1e9}
+
+
 # (n, m, D, projection) of the two-phase sweep; the first is the fused step's shape
 RW_SWEEP = ((4, 1, 768, False), (4, 1, 768, True), (4, 2, 768, False), (4, 4, 512, False), (6, 3, 1024, True),
             (2, 1, 2048, False), (8, 4, 1024, False))
@@ -1093,6 +1109,8 @@ def run_sweep(args):
                           "reference_a100_gbs": ref_gbs, "ratio": gbs / ref_gbs,
                           "reference_source": f"benchmark_small_n_exhaustive_4_3_2026.log:{line_no}"}),
               flush=True)
+    for N, D, proj in BIG_SWEEP:
+        print(json.dumps(large_n_line(device, N, D, proj, steps, args.warmup)), flush=True)
     for n, m, D, proj in RW_SWEEP:
         r = RwRunner(device, TOKENS, n, m, D, proj)
         names = ("read_fwd", "read_bwd", "mix_write_fwd", "mix_write_bwd")
@@ -1133,11 +1151,17 @@ def main():
     ap.add_argument("--n", type=int, default=N_STREAMS, help="with --fused-only: streams (16,384 tokens)")
     ap.add_argument("--block", type=int, default=BLOCK, help="with --fused-only: block size D")
     ap.add_argument("--sweep", action="store_true", help="print the n x D sweep (16,384 tokens) instead")
+    ap.add_argument("--large-n", type=int, default=0,
+                    help="stream_mix_add at this 9 <= n <= 32 alone (2,048 tokens, D = 1536, bf16; ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.sweep:
         run_sweep(args)
+    elif args.large_n:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps(large_n_line(device, args.large_n, 1536, False, args.steps, args.warmup)), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -43,12 +43,9 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
   const int rows = rw_rows(bwd, n, m, mixw);
   if (!ring_geometry(geo, rows, cap, T, D, es, sm_count(), bwd)) return false;
   if (bwd && geo.ns > 1 && rw_gram_mma(n, mixw, es)) {
-    // the Gram on the tensor cores, ring rows padded by 16 bytes (rw_gram_finish)
+    // the Gram on the tensor cores (rw_gram_finish), on swizzled or padded stages
     const WarpGeometry plain = geo;
-    geo.pitch = geo.sl + kGramPad;
-    geo.stage_bytes = rows * geo.pitch * es;
-    geo.gram_mma = kGramPadded;
-    if (!ring_stage(geo, kRwMmaWarps, T, sm_count())) geo = plain;
+    rw_mma_geometry(geo, plain, n, m, T, D, es, true);
   }
   if (bwd && (cap > 8 || geo.gram_mma)) prefer_bwd_consumers(geo, 4);
   if (mixw) prefer_producers(geo);

@@ -415,10 +415,45 @@ constexpr bool rw_gram_mma(int n, bool mixw, int esize) { return mixw && n >= 5 
 // stay in registers (up to 112 floats at n = 8, m = 4), 255 registers a thread.
 constexpr int kRwMmaWarps = 8;
 
-template <typename T, int N, int M, bool PROJ, int W>
+// Geometry of the tensor-core mix-write backward (rw_gram_mma, slices):
+// swizzled TMA stages for even n and D a multiple of 64 (regions g, x of n
+// rows and f of m rows; an odd number of 128-byte lines a row, 9 stages of a
+// kGramBudget ring), else the plain slices in 16-byte padded rows. `plain` is
+// the ring geometry of the shape (rows 2n + m, slices).
+inline bool rw_mma_geometry(WarpGeometry& geo, const WarpGeometry& plain, int n, int m, int64_t T, int64_t D,
+                            int esize, bool allow_swizzle) {
+  if (allow_swizzle && n % 2 == 0 && D % kTmaChunk == 0 && T * n < (int64_t(1) << 31)) {
+    const auto stage_of = [&](int nc) {
+      return 2 * swz_region_bytes(n, nc * kTmaChunk, esize) + swz_region_bytes(m, nc * kTmaChunk, esize);
+    };
+    const int64_t chunks = D / kTmaChunk;
+    int nc_max = 1;
+    for (int c = 3; c <= 255 && stage_of(c) <= kGramBudget / 9; c += 2) nc_max = c;
+    const int64_t ns = (chunks + nc_max - 1) / nc_max;
+    const int nc = static_cast<int>((chunks + ns - 1) / ns) | 1;
+    geo = plain;
+    geo.sl = nc * kTmaChunk;
+    geo.pitch = geo.sl;
+    geo.ns = static_cast<int>((D + geo.sl - 1) / geo.sl);
+    geo.stage_bytes = stage_of(nc);
+    geo.gram_mma = kGramSwizzled;
+    if (geo.ns > 1 && ring_stage(geo, kRwMmaWarps, T, sm_count(), kSwzAlign, kGramBudget)) return true;
+  }
+  geo = plain;
+  geo.pitch = geo.sl + kGramPad;
+  geo.stage_bytes = (2 * n + m) * geo.pitch * esize;
+  geo.gram_mma = kGramPadded;
+  if (ring_stage(geo, kRwMmaWarps, T, sm_count())) return true;
+  geo = plain;
+  return false;
+}
+
+// SWZ: the stage's g region is swizzled (nc lines a row); otherwise row-major
+// with `pitch` elements per row.
+template <typename T, int N, int M, bool PROJ, int W, bool SWZ = false>
 __device__ __forceinline__ void rw_bwd_grads_slice(const RwArgs& a, const RwParams<N, M, true, PROJ>& pr,
                                                    const uint8_t* gsb, int pitch, int64_t t, int64_t d0, int len,
-                                                   int lane) {
+                                                   int lane, int nc = 0) {
   using Wd = Word<T>;
   constexpr int K = Wd::K;
   constexpr int es = sizeof(T);
@@ -432,7 +467,8 @@ __device__ __forceinline__ void rw_bwd_grads_slice(const RwArgs& a, const RwPara
     const uint32_t eo = static_cast<uint32_t>(e0) * es;
     Words<W> gw[N];
 #pragma unroll
-    for (int r = 0; r < N; ++r) gw[r] = lds_words<W>(gsb + eo + r * rowb);
+    for (int r = 0; r < N; ++r)
+      gw[r] = lds_words<W>(stage_at<SWZ>(gsb, rowb, nc, r, static_cast<int>(eo)));
     uint32_t gxo[N][W], gfo[M][W];
 #pragma unroll
     for (int w = 0; w < W; ++w) {
@@ -537,10 +573,11 @@ __device__ __forceinline__ void rw_gram_finish(const RwArgs& a, const RwParams<N
   __syncwarp();
 }
 
-template <typename T, int N, int M, bool MIXW, bool PROJ, bool MMA = false>
+template <typename T, int N, int M, bool MIXW, bool PROJ, bool MMA = false, bool SWZ = false>
 __global__ void __launch_bounds__((MMA ? kRwMmaWarps : rw_bwd_cap(N, M, MIXW, PROJ)) * 32, 1)
-rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
+rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
   static_assert(!MMA || (MIXW && sizeof(T) == 2), "the tensor-core Gram is a mix-write, half-precision path");
+  static_assert(!SWZ || MMA, "swizzled stages belong to the tensor-core Gram");
   using L = RwLayout<N, M, MIXW, PROJ>;
   constexpr int W = MMA ? 2 : rw_bwd_words(N, M, MIXW, PROJ);
   constexpr int NT = (N + M + 7) / 8;
@@ -548,7 +585,10 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   constexpr int es = sizeof(T);
   constexpr int NG = MIXW ? N : M;
   constexpr int NIN = MIXW ? 3 : 2;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // swizzled stages start on a 1024-byte boundary (kSwzAlign bytes of slack)
+  uint8_t* const smem = SWZ ? smem_raw + ((kSwzAlign - (smem_u32(smem_raw) & (kSwzAlign - 1))) & (kSwzAlign - 1))
+                            : smem_raw;
   __shared__ RingState st;
   pdl_launch_dependents();
   ring_init(st, geo.stages);
@@ -568,7 +608,7 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
     if (lane < geo.producers) {
       const void* base[3] = {a.g, a.x, a.f};
       const int rows[3] = {NG, N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
+      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -612,10 +652,15 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
           const uint8_t* gs = sb + tt * NG * rowb;
           const uint8_t* xs = sb + greg + tt * N * rowb;
           const uint8_t* fs = sb + greg + xreg + tt * M * rowb;
+          if constexpr (SWZ) {  // swizzled regions g, x, f (tpi == 1)
+            xs = sb + swz_region_bytes(N, geo.sl, es);
+            fs = xs + swz_region_bytes(N, geo.sl, es);
+          }
           if constexpr (MMA) {
-            rw_bwd_grads_slice<T, N, M, PROJ, W>(a, pr, gs, geo.pitch, t, d0, len, lane);
-            gram_mma_slice<T, N, 0, N, M, false>(cg, gs, nullptr, xs, fs, reinterpret_cast<const uint8_t*>(st.zrow),
-                                                 rowb, 0, len, lane);
+            const int nc = geo.sl / kTmaChunk;
+            rw_bwd_grads_slice<T, N, M, PROJ, W, SWZ>(a, pr, gs, geo.pitch, t, d0, len, lane, nc);
+            gram_mma_slice<T, N, 0, N, M, SWZ>(cg, gs, nullptr, xs, fs, reinterpret_cast<const uint8_t*>(st.zrow),
+                                               rowb, nc, len, lane);
             if (p == ns - 1) {  // token complete
               gram_mma_store<N, N + M>(gram, cg, lane);
               rw_gram_finish<N, M, PROJ>(a, pr, gram, t, lane);
@@ -802,17 +847,38 @@ int rw_launch_one(const WarpGeometry& geo_in, const RwArgs& a, cudaStream_t s) {
   geo.status = timeout_word(s);
   const dim3 block((geo.consumers + 1) * 32, 1, 1);
   if constexpr (BWD) {
+    RingMaps maps{};
     if constexpr (rw_gram_mma(N, MIXW, sizeof(T))) {
-      if (geo.gram_mma) {
+      if constexpr (N % 2 == 0) {
+        if (geo.gram_mma == kGramSwizzled) {
+          const void* base[3] = {a.g, a.x, a.f};
+          const int rows[3] = {N, N, M};
+          if (ring_tensor_maps_swz(geo, maps, base, rows, 3, a.T, a.D, sizeof(T))) {
+            geo.tma = 1;
+            auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ, true, true>;
+            if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
+            return launch_ring(k, geo.grid, (geo.consumers + 1) * 32, geo.smem_bytes, s, a, geo, maps);
+          }
+          // no swizzled maps: the padded rows
+          WarpGeometry plain = geo;
+          if (!ring_geometry(plain, rw_bwd_rows(N, M, MIXW), kRwMmaWarps, a.T, a.D, sizeof(T), sm_count(), true) ||
+              !rw_mma_geometry(geo, plain, N, M, a.T, a.D, sizeof(T), false))
+            return HC_ERR_LAUNCH;
+          geo.status = timeout_word(s);
+          prefer_bwd_consumers(geo, 4);
+          prefer_producers(geo);
+        }
+      }
+      if (geo.gram_mma == kGramPadded) {
         auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ, true>;
         if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-        return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
+        return launch_ring(k, geo.grid, (geo.consumers + 1) * 32, geo.smem_bytes, s, a, geo, maps);
       }
     }
     if (geo.gram_mma) return HC_ERR_LAUNCH;  // not reached: the geometry sets it only for this path
     auto* k = rw_bwd_warp_kernel<T, N, M, MIXW, PROJ>;
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
-    return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo);
+    return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps);
   } else {
     auto* k = rw_fwd_warp_kernel<T, N, M, MIXW, PROJ>;
     if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;

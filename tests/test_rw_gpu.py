@@ -161,9 +161,9 @@ def test_sliced_tokens(n, m, D):
                                         (8, 2, 2048, True)])
 def test_mix_write_sliced_gram(dtype, n, m, D, proj):
     """Half-precision tokens cut into slices at n >= 5: the mix-write
-    backward takes its Gram on the tensor cores (ring rows padded, copied row
-    by row); D = 1800 leaves a last slice that is not a multiple of 16
-    elements."""
+    backward takes its Gram on the tensor cores, on swizzled TMA stages (even
+    n, D a multiple of 64) or 16-byte padded rows copied row by row (odd n,
+    D = 1800, whose last slice is not a multiple of 16 elements)."""
     check_all(*inputs(150, n, m, D, dtype, proj, seed=17 * n + m + D), 2e-2, False)
 
 
