@@ -96,8 +96,8 @@ __host__ __device__ constexpr int swz_region_bytes(int rows, int sl, int esize) 
 // eb / 128, its 16-byte unit (eb / 16) % 8 stored at unit
 // ((eb / 16) % 8) ^ (line % 8).
 __device__ __forceinline__ const uint8_t* swz_at(const uint8_t* region, int nc, int r, int eb) {
-  const int line = r * nc + (eb >> 7);
-  return region + line * 128 + ((((eb >> 4) & 7) ^ (line & 7)) << 4) + (eb & 15);
+  const int off = r * nc * 128 + eb;  // line * 128 + byte in the line
+  return region + (off ^ ((off >> 3) & 0x70));
 }
 
 // 3-D tensor copy global -> this CTA's shared memory through a tensor map in
@@ -1087,7 +1087,7 @@ template <typename T, typename P, int N, bool FUSED, bool PROJ, int W, bool SWZ 
 __device__ __forceinline__ void bwd_grads_slice(const MixBwdArgs& a, const TokParams<P, N, FUSED, PROJ>& pr,
                                                 const uint8_t* gsb, const uint8_t* usb, int pitch, int64_t t,
                                                 int64_t d0, int len, int lane, int nc = 0) {
-  static_assert(!SWZ || (W == 1 && sizeof(T) == 2), "swizzled stages: 4-byte lane reads of 2-byte elements");
+  static_assert(!SWZ || (W <= 2 && sizeof(T) == 2), "swizzled stages: 4- or 8-byte lane reads of 2-byte elements");
   using Wd = Word<T>;
   constexpr int K = Wd::K;
   constexpr int es = sizeof(T);
@@ -1954,7 +1954,9 @@ int launch_mix_fwd_warp(int n, const WarpGeometry& geo_in, const MixFwdArgs& a, 
 template <typename T, typename P, int N, bool FUSED, bool PROJ, bool BLK, bool MMA = false, bool SWZ = false>
 int launch_bwd_kernel(const WarpGeometry& geo, const RingMaps& maps, dim3 block, const MixBwdArgs& a,
                       cudaStream_t s) {
-  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, bwd_lane_words(N, BLK), BLK, MMA, SWZ>;
+  // the tensor-core path reads 8 bytes a lane in pass A (its Gram needs no
+  // registers of sums)
+  auto* k = mix_bwd_warp_kernel<T, P, N, FUSED, PROJ, MMA ? 2 : bwd_lane_words(N, BLK), BLK, MMA, SWZ>;
   if (int rc = warp_prepare(k, geo.smem_bytes)) return rc;
   return launch_ring(k, geo.grid, block, geo.smem_bytes, s, a, geo, maps);
 }

@@ -48,7 +48,11 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
     rw_mma_geometry(geo, plain, n, m, T, D, es, true);
   }
   if (bwd && (cap > 8 || geo.gram_mma)) prefer_bwd_consumers(geo, 4);
-  if (mixw) prefer_producers(geo);
+  if (mixw) {
+    prefer_producers(geo);
+  } else if (mix_tuning().producers > 0) {
+    geo.producers = std::min(mix_tuning().producers, geo.stages);
+  }
   return true;
 }
 
