@@ -1671,7 +1671,7 @@ inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms,
 }
 
 inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T, int64_t D, int esize,
-                          int num_sms, bool bwd) {
+                          int num_sms, bool bwd, int64_t item_bytes = 0) {
   if (T <= 0 || D <= 0 || D % (16 / esize) != 0) return false;
   const MixTuning tune = mix_tuning();
   const int64_t max_stage = 24 * 1024;
@@ -1679,7 +1679,8 @@ inline bool ring_geometry(WarpGeometry& geo, int rows, int warp_cap_, int64_t T,
   // items cap the copy rate (15 KB forward, 16 KB backward measured best; the
   // forward at n = 4, D = 768 takes two 7.5 KB tokens per item: 51.6 against
   // 55.2 us with one)
-  const int64_t item_target = tune.stage_bytes > 0 ? tune.stage_bytes : (bwd ? 16 : 15) * 1024;
+  const int64_t item_target =
+      tune.stage_bytes > 0 ? tune.stage_bytes : item_bytes > 0 ? item_bytes : (bwd ? 16 : 15) * 1024;
   const int64_t tok_bytes = static_cast<int64_t>(rows) * D * esize;
   int64_t sl = D;
   int tpi = 1;
@@ -1749,15 +1750,14 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
                           int esize, int num_sms, int max_gram = kGramSwizzled) {
   const int rows = warp_rows(bwd, fused, n);
   if (!ring_geometry(geo, rows, warp_cap(bwd, n), T, D, esize, num_sms, bwd)) return false;
-  // whole tokens, one a stage, at n = 8 (whose single pass holds every sum in
-  // registers at 8 warps): the blocked path on swizzled stages of at most
-  // 24 KB. Measured on B200 (fused backward, bf16, 16,384 tokens): n = 8,
-  // D = 512 (22.5 KB stages) 99.8 against 116.0 us; larger stages leave too
-  // few consumers (n = 8, D = 640, 26.6 KB: 160.7 against 146.3 us), and at
-  // n = 6 the single pass at 12 warps is as fast or faster (D = 768: 124.1
-  // against 108.6 us).
+  // whole tokens, one a stage, at n = 6 and 8: the blocked path on swizzled
+  // stages of at most 24 KB. Measured on B200 (fused backward, bf16, 16,384
+  // tokens) against the single pass: n = 8, D = 512 89.7 against 116.0 us;
+  // n = 6, D = 384 / 512 / 640 / 768: 61.9 / 69.2 / 85.3 / 97.1 against
+  // 64.5 / 82.6 / 98.5 / 109.6 us. Larger stages leave too few consumers
+  // (n = 8, D = 640, 26.6 KB: 160.7 against 146.3 us).
   constexpr int kWholeMmaMaxStage = 24 * 1024;
-  const bool whole = geo.ns == 1 && geo.tpi == 1 && n == 8;
+  const bool whole = geo.ns == 1 && geo.tpi == 1 && n >= 6;
   if (bwd && gram_mma_dtype(esize) && ((geo.ns > 1 && bwd_blocked(n, proj, geo.ns)) || whole)) {
     // The tensor-core Gram (gram_mma_slice), on swizzled stages for even n
     // and on padded rows for odd n (measured). The swizzled rings take
