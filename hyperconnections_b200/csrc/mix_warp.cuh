@@ -1535,7 +1535,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
-    constexpr bool PAIRS = use_pairs(N);
+    constexpr bool PAIRS = use_pairs(N) && !BLK;  // the blocked path keeps scalar parameters
     constexpr bool BLOCKED = BLK;
     using Params = std::conditional_t<PAIRS, TokParams2<P, N, FUSED, PROJ>, TokParams<P, N, FUSED, PROJ>>;
     Params pr;
@@ -1765,7 +1765,8 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
   // tokens) against the single pass: n = 8, D = 512 89.7 against 116.0 us;
   // n = 6, D = 384 / 512 / 640 / 768: 61.9 / 69.2 / 85.3 / 97.1 against
   // 64.5 / 82.6 / 98.5 / 109.6 us. Larger stages leave too few consumers
-  // (n = 8, D = 640, 26.6 KB: 160.7 against 146.3 us).
+  // (n = 8, D = 640, 26.6 KB: 160.7 against 146.3 us); at n = 4 the single
+  // pass stays faster (D = 768: 70.9 against 74.0 us).
   constexpr int kWholeMmaMaxStage = 24 * 1024;
   const bool whole = geo.ns == 1 && geo.tpi == 1 && n >= 6;
   if (bwd && gram_mma_dtype(esize) && ((geo.ns > 1 && bwd_blocked(n, proj, geo.ns)) || whole)) {
