@@ -1654,6 +1654,8 @@ inline int warp_rows(bool bwd, bool fused, int n) {
 //     one bulk copy per tensor moves several tokens.
 // Stages, consumers and shared memory of the ring for geo.stage_bytes; false
 // when fewer than 3 stages (or no consumer) fit.
+// budget: bytes of stages (200 KB; a 216 KB ring measured no faster for the
+// rings other than the tensor-core Gram's, which take kGramBudget)
 inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms, int slack_bytes = 0,
                        int budget = 200 * 1024) {
   const MixTuning tune = mix_tuning();
