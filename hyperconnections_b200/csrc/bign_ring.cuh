@@ -288,8 +288,8 @@ big_bwd_ring_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const UnitMap um = unit_map(T_, 1);
+  const int ntok = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const int nc = geo.sl / kTmaChunk;
@@ -299,7 +299,7 @@ big_bwd_ring_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     if (lane < geo.producers) {
       const void* base[2] = {a.g, a.x};
       const int rows[2] = {n, n};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, ntok, base, rows, lane, &maps);
+      ring_produce<T, 2>(st, geo, smem, D, um, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -313,7 +313,7 @@ big_bwd_ring_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     for (int g0 = 0; g0 < ntok; g0 += C) {
       const int Wg = min(C, ntok - g0);
       if (c >= Wg) break;
-      const int64_t t = t_begin + g0 + c;
+      const int64_t t = um.tok(g0 + c);
       big_tok_load<T, P, NMAX, PROJ>(a.phi, a.v, t, n, A, vs, cs, lane);  // overlaps the wait for the data
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
@@ -413,8 +413,8 @@ big_fwd_ring_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
+  const UnitMap um = unit_map(T_, 1);
+  const int ntok = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const int nc = geo.sl / kTmaChunk;
@@ -424,7 +424,7 @@ big_fwd_ring_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
     if (lane < geo.producers) {
       const void* base[2] = {a.x, a.src};
       const int rows[2] = {n, n};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, ntok, base, rows, lane, &maps);
+      ring_produce<T, 2>(st, geo, smem, D, um, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -433,7 +433,7 @@ big_fwd_ring_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
     for (int g0 = 0; g0 < ntok; g0 += C) {
       const int Wg = min(C, ntok - g0);
       if (c >= Wg) break;
-      const int64_t t = t_begin + g0 + c;
+      const int64_t t = um.tok(g0 + c);
       big_tok_load<T, P, NMAX, PROJ, false>(a.phi, a.v, t, n, A, warp_vec[c][0], warp_vec[c][1], lane);
       T* ot = static_cast<T*>(a.out) + t * n * D;
       bool ok = true;

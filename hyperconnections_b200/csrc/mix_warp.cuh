@@ -358,11 +358,43 @@ struct ProducerCursor {
 // lane has seen the release of item k - 2S before it waits on the release of
 // item k - S, so a parity wait can never mistake an older phase for the one
 // it waits on.
+#ifndef HC_GRID_STRIDE
+#define HC_GRID_STRIDE 1  // build flag: units dealt to the CTAs grid-strided (1) or in contiguous ranges (0)
+#endif
+
+// The tokens of a CTA's units (tpi consecutive tokens each): unit u starts at
+// token first + u * step, and the CTA's tokens end before `end`.
+//
+// Units are dealt to the CTAs grid-strided: global unit u * G + b goes to CTA
+// b, so at any time the G CTAs stream neighbouring addresses of every tensor
+// instead of G separate ranges. Measured on B200 against contiguous ranges
+// (16,384 tokens, bf16, fused step): forward 43.0 -> 39.0-40.9 us at n = 4,
+// D = 768, -5 to -9% at n = 2..8 over D = 512..4096; backward 0 to -3%;
+// one loss, the n = 6, D = 512 forward (+4%).
+struct UnitMap {
+  int64_t first, step, end;
+  int nunits;
+  __device__ __forceinline__ int64_t tok(int u) const { return first + static_cast<int64_t>(u) * step; }
+  __device__ __forceinline__ int cnt(int u, int tpi) const {
+    return static_cast<int>(min(static_cast<int64_t>(tpi), end - tok(u)));
+  }
+};
+__device__ __forceinline__ UnitMap unit_map(int64_t T, int tpi) {
+  const int64_t G = gridDim.x, b = blockIdx.x;
+  if (HC_GRID_STRIDE) {  // global unit u * G + b
+    const int64_t nu = (T + tpi - 1) / tpi;
+    return UnitMap{b * tpi, G * tpi, T, b < nu ? static_cast<int>((nu - 1 - b) / G + 1) : 0};
+  }
+  const int64_t t0 = T * b / G, t1 = T * (b + 1) / G;  // the CTA's contiguous range
+  return UnitMap{t0, tpi, t1, static_cast<int>((t1 - t0 + tpi - 1) / tpi)};
+}
+
 template <typename T, int NIN>
 __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& geo, uint8_t* smem, int64_t D,
-                                             int64_t t_begin, int ntok, int nunits, const void* const* base,
+                                             const UnitMap& um, const void* const* base,
                                              const int* rows, int lane, const RingMaps* maps = nullptr) {
   const int S = geo.stages, C = geo.consumers, P = geo.producers;
+  const int nunits = um.nunits;
   if (P == 1) {
     int s = 0;
     uint32_t ph = 0;
@@ -381,9 +413,9 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
             fence_proxy_async_smem();
           }
           const int u = g0 + w;
-          const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+          const int cnt = um.cnt(u, geo.tpi);
           ring_issue<T, NIN>(geo, maps, D, smem + static_cast<size_t>(s) * geo.stage_bytes, &st.full[s],
-                             t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, p, base, rows);
+                             um.tok(u), cnt, p, base, rows);
           __threadfence_block();  // the arrive.expect_tx above is visible before the tag
           st.tag[s] = k;
           st.issued[s] = 1;
@@ -412,9 +444,9 @@ __device__ __forceinline__ void ring_produce(RingState& st, const WarpGeometry& 
       }
       if (!fail) {
         const int u = c.g0 + c.w;
-        const int cnt = min(geo.tpi, ntok - u * geo.tpi);
+        const int cnt = um.cnt(u, geo.tpi);
         ring_issue<T, NIN>(geo, maps, D, smem + static_cast<size_t>(c.s) * geo.stage_bytes, &st.full[c.s],
-                           t_begin + static_cast<int64_t>(u) * geo.tpi, cnt, c.p, base, rows);
+                           um.tok(u), cnt, c.p, base, rows);
         st.issued[c.s] = 1;
         st.last_parity[c.s] = c.ph;
         __threadfence_block();  // expect_tx and the drain record are visible before the tag
@@ -812,9 +844,8 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
-  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
+  const UnitMap um = unit_map(T_, geo.tpi);
+  const int nunits = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
@@ -825,7 +856,7 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
     if (lane < geo.producers) {
       const void* base[2] = {a.x, a.src};
       const int rows[2] = {N, NS};
-      ring_produce<T, 2>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
+      ring_produce<T, 2>(st, geo, smem, D, um, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -836,8 +867,8 @@ mix_fwd_warp_kernel(const MixFwdArgs a, const WarpGeometry geo, const __grid_con
       const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
       const int u = g0 + c;
-      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      const int cnt = um.cnt(u, geo.tpi);
+      const int64_t t0 = um.tok(u);
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
@@ -1507,9 +1538,8 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
-  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
+  const UnitMap um = unit_map(T_, geo.tpi);
+  const int nunits = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
@@ -1531,7 +1561,7 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
         rows[2] = 1;
         rows[3] = 1;
       }
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
+      ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -1552,8 +1582,8 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
       const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
       const int u = g0 + c;
-      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      const int cnt = um.cnt(u, geo.tpi);
+      const int64_t t0 = um.tok(u);
       pr.load(a.phi, a.v, a.alpha, a.beta, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {

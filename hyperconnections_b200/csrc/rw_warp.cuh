@@ -167,9 +167,8 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
-  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
+  const UnitMap um = unit_map(T_, geo.tpi);
+  const int nunits = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
@@ -179,7 +178,7 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
     if (lane < geo.producers) {
       const void* base[2] = {a.x, a.f};
       const int rows[2] = {N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane);
+      ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -189,8 +188,8 @@ rw_fwd_warp_kernel(const RwArgs a, const WarpGeometry geo) {
       const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
       const int u = g0 + c;
-      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      const int cnt = um.cnt(u, geo.tpi);
+      const int64_t t0 = um.tok(u);
       pr.load(a, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
@@ -595,9 +594,8 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
   pdl_wait_prior_grid();
 
   const int64_t T_ = a.T, D = a.D;
-  const int64_t t_begin = T_ * blockIdx.x / gridDim.x;
-  const int ntok = static_cast<int>(T_ * (blockIdx.x + 1) / gridDim.x - t_begin);
-  const int nunits = (ntok + geo.tpi - 1) / geo.tpi;
+  const UnitMap um = unit_map(T_, geo.tpi);
+  const int nunits = um.nunits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = geo.stages, C = geo.consumers, ns = geo.ns;
   const uint32_t rowb = static_cast<uint32_t>(geo.pitch) * es;
@@ -608,7 +606,7 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
     if (lane < geo.producers) {
       const void* base[3] = {a.g, a.x, a.f};
       const int rows[3] = {NG, N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, t_begin, ntok, nunits, base, rows, lane, &maps);
+      ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -621,8 +619,8 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
       const int Wg = min(C, nunits - g0);
       if (c >= Wg) break;
       const int u = g0 + c;
-      const int cnt = min(geo.tpi, ntok - u * geo.tpi);
-      const int64_t t0 = t_begin + static_cast<int64_t>(u) * geo.tpi;
+      const int cnt = um.cnt(u, geo.tpi);
+      const int64_t t0 = um.tok(u);
       pr.load(a, t0);  // overlaps the wait for the data
       bool ok = true;
       for (int p = 0; p < ns; ++p) {
