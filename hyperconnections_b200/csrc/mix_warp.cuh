@@ -229,6 +229,7 @@ struct WarpGeometry {
   unsigned int* status; // the library's status word (device-mapped host memory), or nullptr
   int tma;              // slices are copied through the tensor maps (ns > 1 only)
   int gram_mma;         // backward Gram on the tensor cores: 0 no, kGramPadded or kGramSwizzled stages
+  int side;             // fused backward: g_u and f rows fetched by the consumers (side_fetch), not the ring
 };
 
 
@@ -1073,6 +1074,27 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const Params& pr
   }
 }
 
+// Side rows of the fused backward (geo.side): instead of two small bulk
+// copies per item (a bulk copy has a fixed cost, and the g_u / f rows of one
+// token are 1.5 KB at D = 768), each consumer warp copies the g_u and f rows
+// of its next token into one of two slots of its own with 16-byte cp.async
+// while it computes the current token. Slot layout: [g_u row][f row], each
+// D elements. The ring then carries the 2n rows of g and x.
+template <typename T>
+__device__ __forceinline__ void side_fetch(uint8_t* slot, const MixBwdArgs& a, int64_t t, int lane) {
+  const int64_t rowb = a.D * static_cast<int64_t>(sizeof(T));
+  const int chunks = static_cast<int>(rowb / 16);
+  const uint8_t* gu = static_cast<const uint8_t*>(a.gu) + t * rowb;
+  const uint8_t* f = static_cast<const uint8_t*>(a.f) + t * rowb;
+  for (int i = lane; i < chunks; i += 32) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(slot + i * 16)), "l"(gu + i * 16)
+                 : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(slot + rowb + i * 16)), "l"(f + i * 16)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // ------------------------------------------- blocked backward for n >= 5
 // With n >= 5 the per-lane sums of the backward (n^2 + 2n of them) and Phi
 // together no longer leave room for 12 warps. The blocked path splits each
@@ -1561,7 +1583,11 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
         rows[2] = 1;
         rows[3] = 1;
       }
-      ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
+      if (FUSED && geo.side) {
+        ring_produce<T, 2>(st, geo, smem, D, um, base, rows, lane, &maps);
+      } else {
+        ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
+      }
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -1573,6 +1599,17 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     float cg[MMA ? GramMma<N, FUSED>::NT : 1][4];  // tensor-core Gram accumulators of the token
     float2 acc2[PAIRS ? L::kAcc : 1];
     float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
+    // side rows (geo.side: fused, whole tokens one an item): two slots of
+    // this consumer after the ring's stages; the next token's rows are in
+    // flight while a token computes
+    constexpr bool SIDE_OK = FUSED && PAIRS;
+    const bool side = SIDE_OK && geo.side;
+    uint8_t* const side_base =
+        smem + static_cast<size_t>(S) * geo.stage_bytes + static_cast<size_t>(c) * 4 * D * es;
+    int side_slot = 0;
+    if constexpr (SIDE_OK) {
+      if (side && c < nunits) side_fetch<T>(side_base, a, um.tok(c), lane);
+    }
     if constexpr (BLOCKED) {
       for (int k = lane; k < GramShape<N, FUSED>::SIZE; k += 32) gram[k] = 0.f;
       __syncwarp();
@@ -1618,6 +1655,21 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
           const uint8_t* xs = sb + nreg + tt * N * rowb;
           const uint8_t* us = sb + 2 * nreg + tt * rowb;
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
+          if constexpr (SIDE_OK) {
+            if (side) {  // this token's rows landed in its slot; start the next token's
+              uint8_t* cur_slot = side_base + side_slot * 2 * D * es;
+              if (u + C < nunits) {
+                side_fetch<T>(side_base + (side_slot ^ 1) * 2 * D * es, a, um.tok(u + C), lane);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
+              } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+              }
+              __syncwarp();
+              us = cur_slot;
+              fs = cur_slot + D * es;
+              side_slot ^= 1;
+            }
+          }
           if constexpr (SWZ) {  // swizzled regions g, x, g_u, f (tpi == 1)
             const int rn = swz_region_bytes(N, geo.sl, es), r1 = swz_region_bytes(1, geo.sl, es);
             gs = sb;
@@ -1666,6 +1718,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
       }
       if (!ok) break;
     }
+    if constexpr (SIDE_OK) {
+      if (side) asm volatile("cp.async.wait_all;" ::: "memory");  // no copy lands after the CTA is gone
+    }
   }
   ring_drain(st, S);
 }
@@ -1697,6 +1752,7 @@ inline bool ring_stage(WarpGeometry& geo, int warp_cap_, int64_t T, int num_sms,
   geo.stages = stages;
   geo.consumers = consumers;
   geo.producers = 1;
+  geo.side = 0;
   geo.smem_bytes = stages * geo.stage_bytes + slack_bytes;
   geo.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, T)));
   return true;
@@ -1765,6 +1821,13 @@ inline void prefer_bwd_consumers(WarpGeometry& geo, int n) {
     geo.consumers = std::min(geo.consumers, 8);
   }
 }
+
+#ifndef HC_BWD_SIDE
+#define HC_BWD_SIDE 1  // build flag: the fused backward's g_u / f rows by consumer cp.async (side_fetch)
+#endif
+// Dynamic shared memory of a side-row backward (stages + consumer slots;
+// the kernel's static shared memory comes on top, within the 227 KB limit).
+constexpr int kSideSmemBudget = 220 * 1024;
 
 // Producer lanes of the backward rings: four where a fill is small or made of
 // many row copies (a token cut into slices, one copy per row slice; measured
@@ -1853,6 +1916,22 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
     geo.consumers = std::min(geo.consumers, cap - 1);
     if (cap > 8) prefer_bwd_consumers(geo, n);
     prefer_producers(geo);
+    if (fused && use_pairs(n) && geo.ns == 1 && geo.tpi == 1 && !geo.gram_mma && HC_BWD_SIDE) {
+      // side rows (side_fetch): stages of the 2n rows of g and x, then two
+      // slots of g_u / f rows per consumer
+      WarpGeometry sg = geo;
+      const int side_bytes = sg.consumers * 4 * static_cast<int>(D) * esize;
+      sg.stage_bytes = 2 * n * sg.pitch * esize;
+      int stages = std::min(kRingMaxStages, (kSideSmemBudget - side_bytes) / sg.stage_bytes);
+      if (mix_tuning().stages > 0) stages = std::min(stages, mix_tuning().stages);
+      if (stages >= sg.consumers + 2) {
+        sg.stages = stages;
+        sg.smem_bytes = stages * sg.stage_bytes + side_bytes;
+        sg.side = 1;
+        prefer_producers(sg);
+        geo = sg;
+      }
+    }
   } else if (mix_tuning().producers > 0) {
     geo.producers = std::min(mix_tuning().producers, geo.stages);
   }
