@@ -1077,19 +1077,22 @@ __device__ __forceinline__ void bwd_finish(const MixBwdArgs& a, const Params& pr
 // Side rows of the fused backward (geo.side): instead of two small bulk
 // copies per item (a bulk copy has a fixed cost, and the g_u / f rows of one
 // token are 1.5 KB at D = 768), each consumer warp copies the g_u and f rows
-// of its next token into one of two slots of its own with 16-byte cp.async
-// while it computes the current token. Slot layout: [g_u row][f row], each
-// D elements. The ring then carries the 2n rows of g and x.
+// of its next unit (cnt consecutive tokens: contiguous in HBM) into one of
+// two slots of its own with 16-byte cp.async while it computes the current
+// unit. Slot layout: [g_u rows of tpi tokens][f rows of tpi tokens], D
+// elements a row. The ring then carries the 2n rows of g and x.
 template <typename T>
-__device__ __forceinline__ void side_fetch(uint8_t* slot, const MixBwdArgs& a, int64_t t, int lane) {
+__device__ __forceinline__ void side_fetch(uint8_t* slot, const MixBwdArgs& a, int64_t t0, int cnt, int tpi,
+                                           int lane) {
   const int64_t rowb = a.D * static_cast<int64_t>(sizeof(T));
-  const int chunks = static_cast<int>(rowb / 16);
-  const uint8_t* gu = static_cast<const uint8_t*>(a.gu) + t * rowb;
-  const uint8_t* f = static_cast<const uint8_t*>(a.f) + t * rowb;
+  const int chunks = static_cast<int>(cnt * rowb / 16);
+  const uint8_t* gu = static_cast<const uint8_t*>(a.gu) + t0 * rowb;
+  const uint8_t* f = static_cast<const uint8_t*>(a.f) + t0 * rowb;
+  uint8_t* fslot = slot + tpi * rowb;
   for (int i = lane; i < chunks; i += 32) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(slot + i * 16)), "l"(gu + i * 16)
                  : "memory");
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(slot + rowb + i * 16)), "l"(f + i * 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(fslot + i * 16)), "l"(f + i * 16)
                  : "memory");
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -1599,16 +1602,18 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
     float cg[MMA ? GramMma<N, FUSED>::NT : 1][4];  // tensor-core Gram accumulators of the token
     float2 acc2[PAIRS ? L::kAcc : 1];
     float* gram = gram_all + c * GramShape<N, FUSED>::SIZE;
-    // side rows (geo.side: fused, whole tokens one an item): two slots of
-    // this consumer after the ring's stages; the next token's rows are in
-    // flight while a token computes
+    // side rows (geo.side: fused, whole tokens): two slots of this consumer
+    // after the ring's stages; the next unit's rows are in flight while a
+    // unit computes
     constexpr bool SIDE_OK = FUSED && PAIRS;
     const bool side = SIDE_OK && geo.side;
+    const size_t side_slot_bytes = static_cast<size_t>(2) * geo.tpi * D * es;
     uint8_t* const side_base =
-        smem + static_cast<size_t>(S) * geo.stage_bytes + static_cast<size_t>(c) * 4 * D * es;
+        smem + static_cast<size_t>(S) * geo.stage_bytes + static_cast<size_t>(c) * 2 * side_slot_bytes;
     int side_slot = 0;
+    const uint8_t* side_cur = nullptr;  // the current unit's slot
     if constexpr (SIDE_OK) {
-      if (side && c < nunits) side_fetch<T>(side_base, a, um.tok(c), lane);
+      if (side && c < nunits) side_fetch<T>(side_base, a, um.tok(c), um.cnt(c, geo.tpi), geo.tpi, lane);
     }
     if constexpr (BLOCKED) {
       for (int k = lane; k < GramShape<N, FUSED>::SIZE; k += 32) gram[k] = 0.f;
@@ -1656,18 +1661,9 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
           const uint8_t* us = sb + 2 * nreg + tt * rowb;
           const uint8_t* fs = sb + 2 * nreg + oreg + tt * rowb;
           if constexpr (SIDE_OK) {
-            if (side) {  // this token's rows landed in its slot; start the next token's
-              uint8_t* cur_slot = side_base + side_slot * 2 * D * es;
-              if (u + C < nunits) {
-                side_fetch<T>(side_base + (side_slot ^ 1) * 2 * D * es, a, um.tok(u + C), lane);
-                asm volatile("cp.async.wait_group 1;" ::: "memory");
-              } else {
-                asm volatile("cp.async.wait_group 0;" ::: "memory");
-              }
-              __syncwarp();
-              us = cur_slot;
-              fs = cur_slot + D * es;
-              side_slot ^= 1;
+            if (side) {
+              us = side_cur + tt * rowb;
+              fs = side_cur + geo.tpi * rowb + tt * rowb;
             }
           }
           if constexpr (SWZ) {  // swizzled regions g, x, g_u, f (tpi == 1)
@@ -1707,6 +1703,20 @@ mix_bwd_warp_kernel(const MixBwdArgs a, const WarpGeometry geo, const __grid_con
             }
           }
         };
+        if constexpr (SIDE_OK) {
+          if (side) {  // this unit's side rows landed in its slot; start the next unit's
+            side_cur = side_base + side_slot * side_slot_bytes;
+            if (u + C < nunits) {
+              side_fetch<T>(side_base + (side_slot ^ 1) * side_slot_bytes, a, um.tok(u + C), um.cnt(u + C, geo.tpi),
+                            geo.tpi, lane);
+              asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+              asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncwarp();
+            side_slot ^= 1;
+          }
+        }
         if (single) {
           token(0, t0);
         } else {
@@ -1916,17 +1926,27 @@ inline bool warp_geometry(WarpGeometry& geo, bool bwd, bool fused, bool proj, in
     geo.consumers = std::min(geo.consumers, cap - 1);
     if (cap > 8) prefer_bwd_consumers(geo, n);
     prefer_producers(geo);
-    if (fused && use_pairs(n) && geo.ns == 1 && geo.tpi == 1 && !geo.gram_mma && HC_BWD_SIDE) {
+    if (fused && use_pairs(n) && n % 2 == 0 && geo.ns == 1 && geo.tpi == 1 && !geo.gram_mma && HC_BWD_SIDE) {
       // side rows (side_fetch): stages of the 2n rows of g and x, then two
-      // slots of g_u / f rows per consumer
+      // slots of g_u / f rows per consumer; consumers trimmed (at most two)
+      // where the slots would leave fewer than consumers + 2 stages.
+      // Measured on B200 (16,384 tokens, bf16, fused backward) against the
+      // plain ring: n = 4, D = 768 75.7 -> 67.6 us; n = 2, D = 1024 69.8 ->
+      // 56.8 us; n = 4, D = 1024 (7 consumers) 90.3 -> 87.1 us. Not taken
+      // where it measured slower: n = 3, D = 1024 (71.7 -> 74.2 us) and
+      // items of several tokens (n = 4, D = 512: 53.3 -> 55.4 us; n = 1,
+      // D = 1024: 41.0 -> 42.9 us; level at n = 2, 3, D = 512).
       WarpGeometry sg = geo;
-      const int side_bytes = sg.consumers * 4 * static_cast<int>(D) * esize;
-      sg.stage_bytes = 2 * n * sg.pitch * esize;
-      int stages = std::min(kRingMaxStages, (kSideSmemBudget - side_bytes) / sg.stage_bytes);
+      const int slot2 = 4 * sg.tpi * static_cast<int>(D) * esize;  // a consumer's two slots
+      sg.stage_bytes = 2 * n * sg.tpi * sg.pitch * esize;
+      const int fit = (kSideSmemBudget - 2 * sg.stage_bytes) / (slot2 + sg.stage_bytes);
+      const int consumers = std::min(sg.consumers, fit);
+      int stages = consumers > 0 ? std::min(kRingMaxStages, (kSideSmemBudget - consumers * slot2) / sg.stage_bytes) : 0;
       if (mix_tuning().stages > 0) stages = std::min(stages, mix_tuning().stages);
-      if (stages >= sg.consumers + 2) {
+      if (consumers >= 1 && consumers >= sg.consumers - 2 && stages >= consumers + 2) {
+        sg.consumers = consumers;
         sg.stages = stages;
-        sg.smem_bytes = stages * sg.stage_bytes + side_bytes;
+        sg.smem_bytes = stages * sg.stage_bytes + consumers * slot2;
         sg.side = 1;
         prefer_producers(sg);
         geo = sg;
