@@ -95,7 +95,10 @@ def test_fused_fp32(n, D):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("n,D", [(4, 768), (2, 512), (3, 1024), (6, 2048), (8, 4096), (4, 100), (5, 24)])
+# (4, 768), (2, 1024): the backward's side rows; (4, 1024): side rows with the
+# consumers trimmed for their slots; (2, 2048): whole tokens on the plain ring
+@pytest.mark.parametrize("n,D", [(4, 768), (2, 512), (3, 1024), (6, 2048), (8, 4096), (4, 100), (5, 24),
+                                 (4, 1024), (2, 1024), (2, 2048)])
 def test_fused_half(dtype, n, D):
     inputs = workload(29, n, D, dtype, seed=7 * n + D)
     u, x_out, grads = run(*inputs)
@@ -185,7 +188,9 @@ def test_fused_errors():
 
 @pytest.mark.parametrize("n,D,T,dtype", [
     (2, 2048, 4000, torch.bfloat16),   # whole-token stages, several ring rounds per CTA
-    (4, 768, 6000, torch.bfloat16),
+    (4, 768, 6000, torch.bfloat16),    # side rows: g_u / f fetched by the consumers, two slots in turn
+    (4, 1024, 5000, torch.bfloat16),   # side rows, consumers trimmed for their slots
+    (2, 1024, 5000, torch.float16),    # side rows at n = 2
     (3, 1024, 5000, torch.float16),
     (8, 4096, 1200, torch.bfloat16),   # tokens cut into slices
     (6, 2048, 2500, torch.float32),
