@@ -59,6 +59,31 @@ bool ring_ok(WarpGeometry& geo, bool bwd, bool mixw, bool proj, int n, int m, in
   } else if (mix_tuning().producers > 0) {
     geo.producers = std::min(mix_tuning().producers, geo.stages);
   }
+  if (bwd && mixw && !proj && (n == 2 || n == 4) && geo.ns == 1 && geo.tpi == 1 && !geo.gram_mma && HC_BWD_SIDE) {
+    // side rows of f (rw_side_fetch): stages of the 2n rows of g and x, then
+    // two slots of f rows per consumer; consumers trimmed (at most two) where
+    // the slots would leave fewer than consumers + 2 stages. Measured on B200
+    // (16,384 tokens, bf16, mix-write backward) against the plain ring:
+    // n = 4, m = 1, D = 768 73.9 -> 68.5 us; n = 4, m = 2, D = 768 76.6 ->
+    // 71.5 us; n = 2, m = 1, D = 2048 93.8 -> 91.7 us; n = 4, m = 4, D = 512
+    // level; n = 4, m = 1, D = 1024 80.0 -> 83.3 us (a loss kept with the
+    // rule); with the projection 78.7 -> 80.5 us, so not taken there.
+    WarpGeometry sg = geo;
+    const int slot2 = 2 * m * static_cast<int>(D) * es;  // a consumer's two slots
+    sg.stage_bytes = 2 * n * sg.pitch * es;
+    const int fit = (kSideSmemBudget - 2 * sg.stage_bytes) / (slot2 + sg.stage_bytes);
+    const int consumers = std::min(sg.consumers, fit);
+    int stages = consumers > 0 ? std::min(kRingMaxStages, (kSideSmemBudget - consumers * slot2) / sg.stage_bytes) : 0;
+    if (mix_tuning().stages > 0) stages = std::min(stages, mix_tuning().stages);
+    if (consumers >= 1 && consumers >= sg.consumers - 2 && stages >= consumers + 2) {
+      sg.consumers = consumers;
+      sg.stages = stages;
+      sg.smem_bytes = stages * sg.stage_bytes + consumers * slot2;
+      sg.side = 1;
+      prefer_producers(sg);
+      geo = sg;
+    }
+  }
   return true;
 }
 

@@ -572,6 +572,22 @@ __device__ __forceinline__ void rw_gram_finish(const RwArgs& a, const RwParams<N
   __syncwarp();
 }
 
+// Side rows of the mix-write backward (geo.side): the m rows of f of a
+// token (contiguous in HBM) are copied by the consumer warp into one of two
+// slots of its own with 16-byte cp.async while it computes the previous
+// token, instead of riding in the ring as a small bulk copy (see side_fetch,
+// mix_warp.cuh). The ring then carries the 2n rows of g and x.
+template <typename T, int M>
+__device__ __forceinline__ void rw_side_fetch(uint8_t* slot, const RwArgs& a, int64_t t, int lane) {
+  const int64_t bytes = static_cast<int64_t>(M) * a.D * static_cast<int64_t>(sizeof(T));
+  const int chunks = static_cast<int>(bytes / 16);
+  const uint8_t* f = static_cast<const uint8_t*>(a.f) + t * bytes;
+  for (int i = lane; i < chunks; i += 32)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(slot + i * 16)), "l"(f + i * 16)
+                 : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 template <typename T, int N, int M, bool MIXW, bool PROJ, bool MMA = false, bool SWZ = false>
 __global__ void __launch_bounds__((MMA ? kRwMmaWarps : rw_bwd_cap(N, M, MIXW, PROJ)) * 32, 1)
 rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant__ RingMaps maps) {
@@ -606,7 +622,11 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
     if (lane < geo.producers) {
       const void* base[3] = {a.g, a.x, a.f};
       const int rows[3] = {NG, N, M};
-      ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
+      if (MIXW && geo.side) {
+        ring_produce<T, 2>(st, geo, smem, D, um, base, rows, lane, &maps);
+      } else {
+        ring_produce<T, NIN>(st, geo, smem, D, um, base, rows, lane, &maps);
+      }
     }
   } else if (warp - 1 < C) {
     const int c = warp - 1;
@@ -614,6 +634,18 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
     float acc[MMA ? 1 : L::kPad];
     float cg[MMA ? NT : 1][4];  // tensor-core Gram accumulators of the token
     float* gram = gram_all + (MMA ? c * N * (N + M) : 0);
+    // side rows (geo.side: mix-write, whole tokens one an item, no
+    // tensor-core Gram): two slots of this consumer after the ring's stages
+    constexpr bool SIDE_OK = MIXW && !MMA;
+    const bool side = SIDE_OK && geo.side;
+    const size_t side_slot_bytes = static_cast<size_t>(M) * D * es;
+    uint8_t* const side_base =
+        smem + static_cast<size_t>(S) * geo.stage_bytes + static_cast<size_t>(c) * 2 * side_slot_bytes;
+    int side_slot = 0;
+    const uint8_t* side_cur = nullptr;  // the current token's slot
+    if constexpr (SIDE_OK) {
+      if (side && c < nunits) rw_side_fetch<T, M>(side_base, a, um.tok(c), lane);
+    }
     RingCursor cur{c, 0u, c};
     for (int g0 = 0; g0 < nunits; g0 += C) {
       const int Wg = min(C, nunits - g0);
@@ -635,6 +667,19 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
         const uint8_t* sb = smem + static_cast<size_t>(cur.s) * geo.stage_bytes;
         const int64_t d0 = static_cast<int64_t>(p) * geo.sl;
         const int len = static_cast<int>(std::min<int64_t>(geo.sl, D - d0));
+        if constexpr (SIDE_OK) {
+          if (side) {  // this token's f rows landed in its slot; start the next token's
+            side_cur = side_base + side_slot * side_slot_bytes;
+            if (u + C < nunits) {
+              rw_side_fetch<T, M>(side_base + (side_slot ^ 1) * side_slot_bytes, a, um.tok(u + C), lane);
+              asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+              asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncwarp();
+            side_slot ^= 1;
+          }
+        }
         for (int tt = 0; tt < cnt; ++tt) {
           const int64_t t = t0 + tt;
           if (p == 0) {
@@ -650,6 +695,9 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
           const uint8_t* gs = sb + tt * NG * rowb;
           const uint8_t* xs = sb + greg + tt * N * rowb;
           const uint8_t* fs = sb + greg + xreg + tt * M * rowb;
+          if constexpr (SIDE_OK) {
+            if (side) fs = side_cur;  // tpi == 1
+          }
           if constexpr (SWZ) {  // swizzled regions g, x, f (tpi == 1)
             xs = sb + swz_region_bytes(N, geo.sl, es);
             fs = xs + swz_region_bytes(N, geo.sl, es);
@@ -673,6 +721,9 @@ rw_bwd_warp_kernel(const RwArgs a, const WarpGeometry geo, const __grid_constant
         cur.advance(p + 1 < ns ? Wg : C, S);
       }
       if (!ok) break;
+    }
+    if constexpr (SIDE_OK) {
+      if (side) asm volatile("cp.async.wait_all;" ::: "memory");  // no copy lands after the CTA is gone
     }
   }
   ring_drain(st, S);
