@@ -42,6 +42,10 @@ _SIGNATURES = {
     "hc_timeout_status": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "hc_debug_set_mix_tuning": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
     "hc_debug_set_wait_limit": (_c_int, [ctypes.c_uint]),
+    "hc_debug_ring_geometry": (
+        _c_int,
+        [_c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _c_int, ctypes.POINTER(_c_int), _c_int],
+    ),
     "hc_expm_t18_scratch_words": (_c_i64, [_c_i64, _c_int]),
     "hc_expm_t18_fwd": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp, _c_i64, _c_int, _vp]),
     "hc_expm_t18_fwd_noalloc": (_c_int, [_vp, _vp, _c_i64, _c_int, _vp]),

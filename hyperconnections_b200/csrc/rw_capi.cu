@@ -164,3 +164,34 @@ extern "C" int hc_mix_write_bwd(const void* g, const float* H, const void* x, co
                             aligned16(g) && aligned16(x) && aligned16(f) && stream_ok(grad_x) && stream_ok(grad_f));
   return dispatch(true, stream_dtype, ring, true, proj, n, m, geo, a, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" int hc_debug_ring_geometry(int op, int bwd, int n, int m, int proj, int64_t T, int64_t D,
+                                      int stream_dtype, int* out, int out_len) {
+  if (!out) return HC_ERR_NULL_POINTER;
+  if (out_len < 1) return HC_ERR_BAD_SIZE;
+  if (stream_dtype != HC_DTYPE_F32 && stream_dtype != HC_DTYPE_F16 && stream_dtype != HC_DTYPE_BF16)
+    return HC_ERR_DTYPE;
+  if (T <= 0 || D <= 0) return HC_ERR_BAD_SIZE;
+  const int es = dtype_size(stream_dtype);
+  WarpGeometry geo{};
+  bool ring = false;
+  switch (op) {
+    case 0:  // the fused step (m = 1, no projection)
+    case 1:  // stream_mix_add, n <= 8
+      if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
+      ring = D % (16 / es) == 0 &&
+             warp_geometry(geo, bwd != 0, op == 0, op == 1 && proj != 0, n, T, D, es, sm_count());
+      break;
+    case 2:  // read
+    case 3:  // mix-write
+      if (int rc = check_rw(T, n, m, D, stream_dtype)) return rc;
+      ring = ring_ok(geo, bwd != 0, op == 3, op == 3 && proj != 0, n, m, T, D, stream_dtype, true);
+      break;
+    default:
+      return HC_ERR_BAD_SIZE;
+  }
+  const int v[12] = {ring ? 1 : 0, geo.stages, geo.consumers, geo.producers, geo.tpi, geo.sl,
+                     geo.ns, geo.stage_bytes, geo.smem_bytes, geo.side, geo.gram_mma, geo.grid};
+  for (int i = 0; i < out_len && i < 12; ++i) out[i] = ring ? v[i] : 0;
+  return HC_OK;
+}

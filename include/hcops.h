@@ -100,6 +100,21 @@ int hc_debug_set_mix_tuning(int stage_bytes, int stages, int warps, int producer
  * path; the ring's exit drain keeps the default. No reference counterpart. */
 int hc_debug_set_wait_limit(unsigned int polls);
 
+/* DEBUG / TEST HOOK: the ring geometry that the pipelined kernels would take
+ * for one op and shape, by the same host arithmetic the launches use (no
+ * device work; usable without a GPU, where the SM count is taken as 148).
+ * op: 0 the fused step, 1 stream_mix_add (n <= 8), 2 read, 3 mix-write; bwd
+ * non-zero for the backward; m and proj as for the op (ignored where it has
+ * none). Streams are taken as 16-byte aligned. Writes min(out_len, 12) ints:
+ * [ring (1; 0 when the shape takes a non-ring kernel, and every other field
+ * 0), stages, consumer warps, producer lanes, tokens per item, elements per
+ * slice, slices per token, stage bytes, dynamic shared memory bytes, side
+ * rows (1 when the backward's one-row tensors come by consumer copies),
+ * tensor-core Gram stages (0 none, 1 padded, 2 swizzled), CTAs].
+ * Honours hc_debug_set_mix_tuning. No reference counterpart. */
+int hc_debug_ring_geometry(int op, int bwd, int n, int m, int proj, int64_t T,
+                           int64_t D, int stream_dtype, int* out, int out_len);
+
 /* ===========================================================================
  * Batched matrix exponential, n <= 8, float32.
  * ======================================================================== */
