@@ -497,6 +497,50 @@ def time_e2e(device, steps, warmup):
     return e0.elapsed_time(e1) / steps, h2d, d2h
 
 
+def time_host_copies(device, steps, warmup):
+    """The end-to-end leg's host<->device traffic alone, its ceiling: every
+    step copies the same pinned inputs host->device on one stream while
+    output-shaped device buffers are copied device->host on another (both
+    PCIe directions at once, as in time_e2e), with no kernels and no autograd.
+    Returns ms per step."""
+    with numa_local(device.index):
+        host_in = [t.pin_memory() for t in fused_workload(TOKENS, N_STREAMS, BLOCK, seed=1)]
+    x, f, H, a, b, g_u, g_x = host_in
+    # the step's outputs: u, x', grad_x, grad_f, grad_H, grad_alpha, grad_beta
+    dev_in = [torch.empty(t.shape, dtype=t.dtype, device=device) for t in host_in]
+    dev_out = [torch.zeros(t.shape, dtype=t.dtype, device=device) for t in (g_u, g_x, x, f, H, a, b)]
+    with numa_local(device.index):
+        host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dev_out]
+    comp = torch.cuda.current_stream(device)
+    up = torch.cuda.Stream(device)
+    down = torch.cuda.Stream(device)
+
+    def step():
+        with torch.cuda.stream(up):
+            for dst, src in zip(dev_in, host_in):
+                dst.copy_(src, non_blocking=True)
+        with torch.cuda.stream(down):
+            for dst, src in zip(host_out, dev_out):
+                dst.copy_(src, non_blocking=True)
+
+    up.wait_stream(comp)
+    down.wait_stream(comp)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    up.wait_stream(comp)
+    down.wait_stream(comp)
+    for _ in range(steps):
+        step()
+    comp.wait_stream(up)
+    comp.wait_stream(down)
+    e1.record(comp)
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1) / steps
+
+
 # ---------------------------------------------------------------- CPU baseline
 def reference_cpu_path():
     """The reference's own eager CPU path for the fused step and for
@@ -741,6 +785,15 @@ def run_b200(args):
     e2e_ms, h2d, d2h = time_e2e(device, max(3, min(args.steps, 20)), 2)
     e2e_ms_max = max_over_ranks(e2e_ms, world, device)
     e2e_value = world * (fb + bb) / (e2e_ms_max * 1e-3) / 1e9
+    # the same copies without the step: the ceiling the host link puts on e2e
+    # at this N (every rank copies at once); context only, so a failure here
+    # records its reason instead of ending the run
+    copy_err = None
+    try:
+        copy_ms = time_host_copies(device, max(3, min(args.steps, 20)), 2)
+    except Exception as exc:  # noqa: BLE001
+        copy_ms, copy_err = float("nan"), f"{type(exc).__name__}: {exc}"[:200]
+    copy_ms_max = max_over_ranks(copy_ms, world, device)
     sampler.stop()
 
     models = {}
@@ -795,7 +848,13 @@ def run_b200(args):
             "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_ms_max,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "hyperconnections_b200.ops.stream_mix_fused + autograd, pinned host buffers, "
-                            "upload of step i+1 overlapping download of step i"},
+                            "upload of step i+1 overlapping download of step i",
+                    "copy_ceiling": ({"value": world * (fb + bb) / (copy_ms_max * 1e-3) / 1e9, "unit": "GB/s",
+                                      "ms_per_step": copy_ms_max,
+                                      "what": "the same H2D and D2H copies per step on two streams at once, "
+                                              "no kernels, every rank at once"}
+                                     if copy_ms_max == copy_ms_max and copy_ms_max > 0
+                                     else {"unavailable": copy_err or "no finite time"})},
             "gpu_launches": res["launches"],
             "clocks": clocks,
         }
