@@ -6,6 +6,7 @@
 // elements and every stream base is 16-byte aligned; any other shape runs
 // the element-wise kernels of the same arithmetic.
 #include "rw_warp.cuh"
+#include "bign_ring.cuh"  // big_ring_geometry (hc_debug_ring_geometry)
 
 namespace hc {
 namespace {
@@ -177,7 +178,11 @@ extern "C" int hc_debug_ring_geometry(int op, int bwd, int n, int m, int proj, i
   bool ring = false;
   switch (op) {
     case 0:  // the fused step (m = 1, no projection)
-    case 1:  // stream_mix_add, n <= 8
+    case 1:  // stream_mix_add
+      if (op == 1 && n > 8 && n <= kBigMaxN) {  // 9 <= n <= 32: the tensor-core ring (half precision)
+        ring = es == 2 && HC_GRAM_MMA && big_ring_geometry(geo, n, T, D);
+        break;
+      }
       if (n < 1 || n > 8) return HC_ERR_UNSUPPORTED_N;
       ring = D % (16 / es) == 0 &&
              warp_geometry(geo, bwd != 0, op == 0, op == 1 && proj != 0, n, T, D, es, sm_count());

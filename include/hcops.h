@@ -103,7 +103,9 @@ int hc_debug_set_wait_limit(unsigned int polls);
 /* DEBUG / TEST HOOK: the ring geometry that the pipelined kernels would take
  * for one op and shape, by the same host arithmetic the launches use (no
  * device work; usable without a GPU, where the SM count is taken as 148).
- * op: 0 the fused step, 1 stream_mix_add (n <= 8), 2 read, 3 mix-write; bwd
+ * op: 0 the fused step, 1 stream_mix_add (n <= 32; above 8 the
+ * half-precision tensor-core ring, the same for both directions), 2 read,
+ * 3 mix-write; bwd
  * non-zero for the backward; m and proj as for the op (ignored where it has
  * none). Streams are taken as 16-byte aligned. Writes min(out_len, 12) ints:
  * [ring (1; 0 when the shape takes a non-ring kernel, and every other field

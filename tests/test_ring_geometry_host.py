@@ -42,6 +42,8 @@ def cases():
                     yield (0, bwd, n, 1, False, D, dtype)
                     for proj in (False, True):
                         yield (1, bwd, n, 1, proj, D, dtype)
+                for n in (9, 12, 16, 24, 32):  # stream_mix_add on the tensor-core ring (bf16 only)
+                    yield (1, bwd, n, 1, False, D, dtype)
                 for n, m in ((2, 1), (4, 1), (4, 2), (4, 4), (6, 3), (8, 4)):
                     yield (2, bwd, n, m, False, D, dtype)
                     for proj in (False, True):
@@ -84,6 +86,16 @@ def test_side_rows_where_measured(lib):
     assert geometry(lib, 1, 1, 4, 768)["side"] == 0        # stream_mix_add
 
 
+def test_large_n_ring(lib):
+    for n in (9, 16, 32):
+        g = geometry(lib, 1, 1, n, 1536)
+        assert g["ring"] and g["gram_mma"] == 2 and g["consumers"] == 7 and g["stages"] >= 9, (n, g)
+        # stages and 1 KB of alignment slack within the tensor-core rings' 216 KB budget
+        assert g["smem_bytes"] <= 216 * 1024 + 1024, (n, g)
+    assert not geometry(lib, 1, 1, 16, 1536, dtype="f32")["ring"]  # fp32 streams take the CUDA-core kernels
+    assert not geometry(lib, 1, 1, 16, 100)["ring"]                # D not a multiple of 64
+
+
 def test_tuning_hook_reaches_the_side_rows(lib):
     try:
         assert lib.hc_debug_set_mix_tuning(0, 3, 1, 0) == 0
@@ -96,6 +108,7 @@ def test_tuning_hook_reaches_the_side_rows(lib):
 def test_rejects_bad_arguments(lib):
     out = (ctypes.c_int * len(FIELDS))()
     assert lib.hc_debug_ring_geometry(0, 1, 9, 1, 0, TOKENS, 768, _lib.HC_DTYPE_BF16, out, len(FIELDS)) != 0
+    assert lib.hc_debug_ring_geometry(1, 1, 33, 1, 0, TOKENS, 768, _lib.HC_DTYPE_BF16, out, len(FIELDS)) != 0
     assert lib.hc_debug_ring_geometry(7, 1, 4, 1, 0, TOKENS, 768, _lib.HC_DTYPE_BF16, out, len(FIELDS)) != 0
     assert lib.hc_debug_ring_geometry(0, 1, 4, 1, 0, 0, 768, _lib.HC_DTYPE_BF16, out, len(FIELDS)) != 0
     assert lib.hc_debug_ring_geometry(0, 1, 4, 1, 0, TOKENS, 768, 9, out, len(FIELDS)) != 0
